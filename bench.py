@@ -1,0 +1,517 @@
+"""Benchmark of the Loom hot path on B200: effective HBM GB/s per generated
+kernel at N = 2^28 fp32 per GPU, 1..8 GPUs (one process per GPU).
+
+One step = one call of each of the seven suite entries (saxpy, relu, dot,
+l2_norm_sq, max_value, affine_relu, pipeline_sum), each over N = 2^28
+float32 elements per GPU (weak scaling: every GPU owns its own N-element
+shards; maps need no communication, each reduction adds one scalar NCCL
+collective).  `value` is the whole-job effective bandwidth: algorithmic bytes
+(every input read once, every tensor output written once) of all ranks per
+step / the step time (max over ranks, CUDA events, inputs resident in HBM).
+Every input is 1 GiB, far larger than the 126 MB L2, so no flush is needed
+between launches.
+
+`e2e` is the same metric through the reference-facing C-ABI entry (the
+synchronous `loom_kernels_<entry>` call) with pinned HOST buffers: every
+step copies each entry's inputs host->device, calls the entry, and copies the
+result back.
+
+`--impl reference` times the reference's CPU semantics for the same workload
+on this machine's host cores (the C oracle: the reference has no CPU
+implementation of this path and its OCaml compiler cannot be built here),
+on a bounded sample of N per step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "Effective HBM GB/s & % of B200 peak per kernel, N=2^28 fp32, at 1/2/4/8 GPUs"
+ENTRIES = ["saxpy", "relu", "dot", "l2_norm_sq", "max_value", "affine_relu", "pipeline_sum"]
+# tensor params per entry, their data source, and algorithmic bytes per element
+TENSORS = {
+    "saxpy": ("u0", "u1"), "relu": ("nrm",), "dot": ("u0", "u1"), "l2_norm_sq": ("outl",),
+    "max_value": ("outl",), "affine_relu": ("u0", "u1"), "pipeline_sum": ("u0", "u1", "u2"),
+}
+PARAM_NAMES = {
+    "saxpy": ("x", "y"), "relu": ("x",), "dot": ("x", "y"), "l2_norm_sq": ("x",),
+    "max_value": ("x",), "affine_relu": ("x", "y"), "pipeline_sum": ("x", "y", "w"),
+}
+SCALARS = {"saxpy": {"a": 2.5}, "affine_relu": {"a": 0.75}, "pipeline_sum": {"a": 0.75}}
+MAP_ENTRIES = {"saxpy", "relu", "affine_relu"}
+FALLBACK_HBM_GBS = 6650.0
+
+
+def bytes_per_elem(entry: str) -> int:
+    return 4 * (len(TENSORS[entry]) + (1 if entry in MAP_ENTRIES else 0))
+
+
+def read_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "of measured"
+    except (OSError, ValueError, KeyError):
+        return FALLBACK_HBM_GBS, "of fallback"
+
+
+def read_traffic():
+    """Per-launch DRAM bytes of each kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as fh:
+            return json.load(fh)
+    except (OSError, ValueError):
+        return {}
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", self.gpu_id],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(power) if power else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def setup_dist(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(world, value: float) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gather_obj(world, obj):
+    if world == 1:
+        return [obj]
+    import torch.distributed as dist
+    out = [None] * world
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def make_inputs(n: int, rank: int):
+    """Seeded device inputs of the suite (uniform x3, normal, normal+outliers)."""
+    import torch
+    from loom_b200.workloads import BASE_SEED, INPUT_SEED_STRIDE
+    gen = torch.Generator(device="cuda")
+    data = {}
+    for k, name in enumerate(("u0", "u1", "u2")):
+        gen.manual_seed(BASE_SEED + k * INPUT_SEED_STRIDE + rank * 7919)
+        t = torch.rand(n, device="cuda", dtype=torch.float32, generator=gen)
+        data[name] = t.mul_(2.0).sub_(1.0)
+    gen.manual_seed(BASE_SEED + 3 * INPUT_SEED_STRIDE + rank * 7919)
+    data["nrm"] = torch.randn(n, device="cuda", dtype=torch.float32, generator=gen)
+    gen.manual_seed(BASE_SEED + 4 * INPUT_SEED_STRIDE + rank * 7919)
+    outl = torch.randn(n, device="cuda", dtype=torch.float32, generator=gen)
+    mask = torch.rand(n, device="cuda", generator=gen) < 0.01   # seeded 1% outliers
+    outl[mask] *= 1e3
+    data["outl"] = outl
+    del mask
+    return data
+
+
+def launches_per_call(entry: str, world: int) -> int:
+    if entry in MAP_ENTRIES:
+        return 1
+    if world == 1:
+        return 2
+    return 3 if entry != "max_value" else 2  # + rank fold kernel for sums
+
+
+def run_ours(args) -> None:
+    import ctypes
+
+    import torch
+    from loom_b200.build import load_suite
+
+    world, rank, local = setup_dist(args)
+    pkg = load_suite()
+    n = 1 << args.n_log2
+    peak, peak_src = read_peak()
+    data = make_inputs(n, rank)
+    outs = {e: torch.empty(n if e in MAP_ENTRIES else 1, device="cuda") for e in ENTRIES}
+    comm = pkg.comm_from_process_group() if world > 1 else None
+    stream = torch.cuda.current_stream()
+
+    # Pre-bind every call (no Python tensor work inside the timed loop).
+    calls = []
+    for e in ENTRIES:
+        ent = pkg[e]
+        args_c = []
+        tens = dict(zip(PARAM_NAMES[e], TENSORS[e]))
+        for p in ent.params:
+            if p["kind"] == "scalar-f32":
+                args_c.append(ctypes.c_float(SCALARS[e][p["name"]]))
+            else:
+                args_c.append(ctypes.c_void_p(data[tens[p["name"]]].data_ptr()))
+        if world > 1:
+            ws = ent.workspace(n, dist=True)
+            tail = [ctypes.c_int64(n), ctypes.c_void_p(outs[e].data_ptr()),
+                    ctypes.c_void_p(ws.data_ptr()) if ws is not None else None,
+                    ctypes.c_size_t(ws.numel() if ws is not None else 0),
+                    ctypes.c_void_p(comm.handle), ctypes.c_void_p(stream.cuda_stream)]
+            fn = ent.dist_fn
+        else:
+            ws = ent.workspace(n)
+            tail = [ctypes.c_int64(n), ctypes.c_void_p(outs[e].data_ptr()),
+                    ctypes.c_void_p(ws.data_ptr()) if ws is not None else None,
+                    ctypes.c_size_t(ws.numel() if ws is not None else 0),
+                    ctypes.c_void_p(stream.cuda_stream)]
+            fn = ent.stream_fn
+        calls.append((e, fn, args_c + tail))
+
+    def step(events=None):
+        for i, (e, fn, a) in enumerate(calls):
+            if events is not None:
+                events[i][0].record(stream)
+            st = fn(*a)
+            if st != 0:
+                raise RuntimeError(f"{e} returned status {st}")
+            if events is not None:
+                events[i][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+
+    props = torch.cuda.get_device_properties(local)
+    sampler = ClockSampler(f"GPU-{props.uuid}" if hasattr(props, "uuid") else str(local))
+    sampler.start()
+    time.sleep(0.3)
+    per_kernel = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in calls] for _ in range(args.steps)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for s in range(args.steps):
+        step(per_kernel[s])
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    clocks = sampler.stop()
+    elapsed_ms = start.elapsed_time(end)
+    kernel_ms = {e: sum(per_kernel[s][i][0].elapsed_time(per_kernel[s][i][1])
+                        for s in range(args.steps)) / args.steps
+                 for i, (e, _, _) in enumerate(calls)}
+    elapsed_ms = max_over_ranks(world, elapsed_ms)
+    ms_per_step = elapsed_ms / args.steps
+    step_bytes = sum(bytes_per_elem(e) for e in ENTRIES) * n
+    value = step_bytes * world / (ms_per_step * 1e-3) / 1e9
+
+    # e2e through the reference-facing synchronous entry with pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(pkg, data, outs, n, args, world, comm)
+    all_clocks = gather_obj(world, clocks)
+    all_kernels = gather_obj(world, kernel_ms)
+
+    if rank == 0:
+        traffic = read_traffic()
+        kernels = {}
+        for e in ENTRIES:
+            ms = max(k[e] for k in all_kernels)
+            gbs = bytes_per_elem(e) * n / (ms * 1e-3) / 1e9
+            kernels[e] = {"us_per_call": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+                          "frac": round(gbs / peak, 4), "bytes_per_elem": bytes_per_elem(e)}
+        dom = max(ENTRIES, key=lambda e: kernels[e]["us_per_call"])
+        dom_bytes = bytes_per_elem(dom) * n
+        dom_traffic = traffic.get(dom, {}).get("dram_bytes_per_launch_at_2^28")
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded U(-1,1), N(0,1), N(0,1) with 1% x1e3 outliers)",
+            "pct_of_peak": round(100 * value / (peak * world), 2),
+            "config": {
+                "workload": ("b200_suite step: saxpy, relu, dot, l2_norm_sq, max_value, "
+                             "affine_relu, pipeline_sum, each over N=2^%d fp32 per GPU"
+                             % args.n_log2),
+                "n_per_gpu": n,
+                "global_n": n * world,
+                "entries": ENTRIES,
+                "l2": "no flush: every input is 1 GiB per GPU (> 126 MB L2)",
+                "parallelism": f"shard{world} (maps: no communication; reductions: one "
+                               "scalar NCCL collective)",
+            },
+            "kernels": kernels,
+            "roofline": {
+                "bound": "hbm",
+                "kernel": dom,
+                "achieved": round(dom_bytes / (kernels[dom]["us_per_call"] * 1e-6) / 1e9, 1),
+                "peak": peak,
+                "peak_source": peak_src,
+                "unit": "GB/s",
+                "frac": round(dom_bytes / (kernels[dom]["us_per_call"] * 1e-6) / 1e9 / peak, 4),
+                "traffic": dom_traffic,
+                "algorithmic_bytes_per_launch": dom_bytes,
+            },
+            "clocks": {
+                "sm_mhz": all_clocks[0]["sm_mhz"],
+                "sm_max_mhz": all_clocks[0]["sm_max_mhz"],
+                "reasons": sorted({r for c in all_clocks for r in c["reasons"]}),
+                "per_rank_sm_mhz": [c["sm_mhz"] for c in all_clocks],
+            },
+            "gpu_launches": args.steps * sum(launches_per_call(e, world) for e in ENTRIES),
+            "e2e": e2e,
+        }
+        if world == 1 and not args.no_cpu:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_log2, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if comm is not None:
+        comm.destroy()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def run_e2e(pkg, data, outs, n, args, world, comm):
+    """Reference-facing synchronous entries (the _dist entries across GPUs),
+    pinned host inputs, D2H results."""
+    import ctypes
+
+    import torch
+    host = {k: torch.empty(n, dtype=torch.float32, pin_memory=True) for k in data}
+    for k, v in data.items():
+        host[k].copy_(v)
+    host_out = {e: torch.empty(n if e in MAP_ENTRIES else 1, dtype=torch.float32,
+                               pin_memory=True) for e in ENTRIES}
+    stream = torch.cuda.current_stream()
+    h2d = sum(4 * n * len(TENSORS[e]) for e in ENTRIES)
+    d2h = sum(4 * (n if e in MAP_ENTRIES else 1) for e in ENTRIES)
+
+    def step():
+        for e in ENTRIES:
+            ent = pkg[e]
+            used = set(TENSORS[e])
+            for k in used:
+                data[k].copy_(host[k], non_blocking=True)
+            args_c = []
+            tens = dict(zip(PARAM_NAMES[e], TENSORS[e]))
+            for p in ent.params:
+                if p["kind"] == "scalar-f32":
+                    args_c.append(ctypes.c_float(SCALARS[e][p["name"]]))
+                else:
+                    args_c.append(ctypes.c_void_p(data[tens[p["name"]]].data_ptr()))
+            ws = ent.workspace(n, dist=world > 1)
+            tail = [ctypes.c_int64(n), ctypes.c_void_p(outs[e].data_ptr()),
+                    ctypes.c_void_p(ws.data_ptr()) if ws is not None else None,
+                    ctypes.c_size_t(ws.numel() if ws is not None else 0)]
+            if world > 1:
+                st = ent.dist_fn(*args_c, *tail, ctypes.c_void_p(comm.handle),
+                                 ctypes.c_void_p(stream.cuda_stream))
+            else:
+                st = ent.fn(*args_c, *tail)
+            if st != 0:
+                raise RuntimeError(f"{e} returned status {st}")
+            host_out[e].copy_(outs[e], non_blocking=True)
+        stream.synchronize()
+
+    steps = max(1, args.e2e_steps)
+    step()
+    torch.cuda.synchronize()
+    barrier(world)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        step()
+    end.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(world, start.elapsed_time(end)) / steps
+    step_bytes = sum(bytes_per_elem(e) for e in ENTRIES) * n
+    return {"value": round(step_bytes * world / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
+            "ms_per_step": round(ms, 3),
+            "path": "loom_kernels_<entry> (synchronous reference ABI), pinned host buffers"}
+
+
+def cpu_baseline(log2n: int, seconds: float, threads: int = 0):
+    """The C oracle (the reference's per-element semantics, OpenMP) on the
+    host cores, on N=2^log2n per entry; reports effective GB/s."""
+    import numpy as np
+    from loom_b200 import workloads
+    from oracle.loom_oracle import Oracle, load_programs
+    threads = threads or len(os.sched_getaffinity(0))
+    oracle = Oracle(load_programs(os.path.join(ROOT, "loom_b200", "suite",
+                                               "kernels.tensor_ir.json")), name="b200_suite")
+    n = 1 << log2n
+    inputs = {e: workloads.entry_inputs(e, n) for e in ENTRIES}
+    for e in ENTRIES:
+        oracle.run(e, inputs[e], threads=threads)
+    reps, total = 0, 0.0
+    t0 = time.perf_counter()
+    while True:
+        for e in ENTRIES:
+            oracle.run(e, inputs[e], threads=threads)
+        reps += 1
+        total = time.perf_counter() - t0
+        if total >= seconds:
+            break
+    step_bytes = sum(bytes_per_elem(e) for e in ENTRIES) * n
+    return {"value": round(step_bytes * reps / total / 1e9, 2), "unit": "GB/s",
+            "cores": threads, "kind": "port",
+            "sample": f"the 7 suite entries at N=2^{log2n} each, {reps} steps in {total:.1f} s",
+            "seconds": round(total, 2)}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    base = cpu_baseline(args.cpu_log2, args.cpu_seconds)
+    # time exactly --steps steps of the bounded sample after --warmup
+    import numpy as np
+    from loom_b200 import workloads
+    from oracle.loom_oracle import Oracle, load_programs
+    threads = base["cores"]
+    oracle = Oracle(load_programs(os.path.join(ROOT, "loom_b200", "suite",
+                                               "kernels.tensor_ir.json")), name="b200_suite")
+    n = 1 << args.cpu_log2
+    inputs = {e: workloads.entry_inputs(e, n) for e in ENTRIES}
+    for _ in range(args.warmup):
+        for e in ENTRIES:
+            oracle.run(e, inputs[e], threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for e in ENTRIES:
+            oracle.run(e, inputs[e], threads=threads)
+    total = time.perf_counter() - t0
+    step_bytes = sum(bytes_per_elem(e) for e in ENTRIES) * n
+    value = step_bytes * args.steps / total / 1e9
+    print(json.dumps({
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded U(-1,1), N(0,1), N(0,1) with 1% x1e3 outliers)",
+        "config": {"workload": ("b200_suite step: saxpy, relu, dot, l2_norm_sq, max_value, "
+                                "affine_relu, pipeline_sum on the host cores, bounded sample "
+                                "N=2^%d per entry (GPU arm: N=2^28 per GPU)" % args.cpu_log2),
+                   "n_per_step": n, "entries": ENTRIES},
+        "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"the 7 suite entries at N=2^{args.cpu_log2} each per step"},
+        "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n-log2", type=int, default=28)
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-log2", type=int, default=24)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,362 @@
+"""Package and compile drivers: TensorIR entries -> lib<project>.so + header,
+manifest, report and per-entry plan dumps.
+
+Follows the artefact layout of the reference's CUDA packaging
+(``src/loom_backend_cuda/cuda_backend.ml:2675-2816``):
+
+* ``package``: ``<out>/include/loom/<pkg>.h``, ``<out>/src-gen/<pkg>.cu``,
+  ``<out>/lib<pkg>.so`` (or ``.a``), ``<out>/manifest.json``,
+  ``<out>/report.md`` and ``<out>/entries/<symbol>/*``;
+* ``compile``: ``<out>/<entry>_cuda.h``, ``<out>/<entry>_cuda.cu``,
+  ``<out>/lib<entry>.so``, ``manifest.json``, ``report.md``.
+
+The nvcc line targets sm_100a only (``-gencode arch=compute_100a,
+code=sm_100a``) and adds ``-fmad=false`` (see ``render.py``) and the NCCL
+link for the multi-GPU entries.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+import shlex
+import shutil
+import subprocess
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Iterable, List, Optional, Sequence
+
+from . import codegen
+from .plan import EntryPlan, plan_entry, plan_to_json, sanitize_ident
+from .tensor_ir import Program, TensorIRError, program_from_json, program_to_string
+
+CSRC = Path(__file__).resolve().parent / "csrc"
+CUDA_ARCH = "sm_100a"
+GENCODE = "arch=compute_100a,code=sm_100a"
+
+# Reference optimisation flags that change this backend's output.  Every other
+# flag is accepted and recorded; the B200 plan (always fused, always
+# vectorised, deterministic two-launch reductions) does not depend on it.
+HONOURED_FLAGS = {"cuda-async-wrapper-return"}
+
+
+class BuildError(RuntimeError):
+    pass
+
+
+@dataclass
+class Options:
+    enabled: List[str] = field(default_factory=list)
+    multi_gpu: bool = True
+    kind: str = "shared"          # "shared" | "static"
+    nvcc: str = "nvcc"
+    extra_nvcc_flags: List[str] = field(default_factory=list)
+
+    @property
+    def async_return(self) -> bool:
+        return "cuda-async-wrapper-return" in self.enabled
+
+    def to_json(self) -> dict:
+        return {"enabled": sorted(set(self.enabled)),
+                "honoured": sorted(set(self.enabled) & HONOURED_FLAGS),
+                "no_effect_on_b200_plan": sorted(set(self.enabled) - HONOURED_FLAGS)}
+
+
+@dataclass
+class EntryBundle:
+    module_name: str
+    source_file: str
+    program: Program
+    plan: EntryPlan
+
+
+def module_name_of_file(path: str) -> str:
+    base = os.path.basename(path)
+    for suffix in (".tensor_ir.json", ".json", ".py", ".ml", ".cpp"):
+        if base.endswith(suffix):
+            base = base[: -len(suffix)]
+            break
+    return sanitize_ident(base)
+
+
+def load_entries_file(path: str) -> List[Program]:
+    """A ``*.tensor_ir.json`` file holds one TensorIR program or a list."""
+    with open(path, "r", encoding="utf-8") as fh:
+        obj = json.load(fh)
+    items = obj if isinstance(obj, list) else [obj]
+    return [program_from_json(item) for item in items]
+
+
+def discover_entries(project_root: str, module_filters: Sequence[str] = (),
+                     entry_filters: Sequence[str] = ()) -> List[EntryBundle]:
+    """Collect entries of a project (cuda_backend.ml:158-178, 307-326): every
+    ``*.tensor_ir.json`` below the root, skipping build and hidden dirs."""
+    skip = {"_build", "build", ".venv", ".git", ".hg", ".svn", "node_modules"}
+    found: List[str] = []
+    for dirpath, dirnames, filenames in os.walk(project_root):
+        dirnames[:] = sorted(d for d in dirnames if d not in skip and not d.startswith("."))
+        for name in sorted(filenames):
+            if name.endswith(".tensor_ir.json"):
+                found.append(os.path.join(dirpath, name))
+    mfilt = [m.lower() for m in module_filters]
+    efilt = [e.lower() for e in entry_filters]
+    bundles: List[EntryBundle] = []
+    for path in found:
+        module = module_name_of_file(path)
+        if mfilt and module.lower() not in mfilt:
+            continue
+        for prog in load_entries_file(path):
+            if efilt and prog.entry_name.lower() not in efilt:
+                continue
+            bundles.append(EntryBundle(module, path, prog, plan_entry(prog, module)))
+    return bundles
+
+
+def package_name_of_root(root: str) -> str:
+    """``loom-package.json`` name, else the directory name (cuda_backend.ml:192-208)."""
+    marker = os.path.join(root, "loom-package.json")
+    if os.path.exists(marker):
+        try:
+            with open(marker, "r", encoding="utf-8") as fh:
+                name = json.load(fh).get("name", "")
+            if isinstance(name, str) and name.strip():
+                return sanitize_ident(name)
+        except (OSError, ValueError):
+            pass
+    return sanitize_ident(os.path.basename(os.path.abspath(root)))
+
+
+def nvcc_command(opts: Options, include_dir: str, source: str, artifact: str,
+                 object_only: bool = False) -> List[str]:
+    cmd = [opts.nvcc, "-std=c++17", "-O3", "-gencode", GENCODE, "-fmad=false", "-lineinfo",
+           "-Xptxas", "-O3", f"-I{include_dir}", f"-I{CSRC}"]
+    if object_only:
+        cmd += ["-c", "-Xcompiler", "-fPIC", "-o", artifact, source]
+    else:
+        cmd += ["-shared", "-Xcompiler", "-fPIC", "-o", artifact, source]
+        if opts.multi_gpu:
+            cmd.append("-lnccl")
+    return cmd + list(opts.extra_nvcc_flags)
+
+
+def _run(cmd: List[str]) -> None:
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise BuildError(f"command failed ({proc.returncode}): {shlex.join(cmd)}\n"
+                         f"{proc.stdout}\n{proc.stderr}")
+
+
+def build_artifact(opts: Options, include_dir: str, source: str, artifact: str) -> List[str]:
+    if shutil.which(opts.nvcc) is None and not os.path.exists(opts.nvcc):
+        raise BuildError("nvcc is required on PATH for the Loom B200 backend")
+    if opts.kind == "shared":
+        cmd = nvcc_command(opts, include_dir, source, artifact)
+        _run(cmd)
+        return [shlex.join(cmd)]
+    obj = os.path.splitext(source)[0] + ".o"
+    cmd = nvcc_command(opts, include_dir, source, obj, object_only=True)
+    _run(cmd)
+    ar = ["ar", "rcs", artifact, obj]
+    _run(ar)
+    return [shlex.join(cmd), shlex.join(ar)]
+
+
+def _entry_json(b: EntryBundle, files: List[str], package: str, multi_gpu: bool) -> dict:
+    p = b.plan
+    d = {
+        "entry_name": b.program.entry_name,
+        "module_name": b.module_name,
+        "source_file": b.source_file,
+        "symbol_name": p.symbol,
+        "workspace_symbol": p.workspace_symbol,
+        "result_kind": b.program.result_kind,
+        "params": [{"name": q.name, "kind": "scalar-f32"} if not hasattr(q, "shape_symbol")
+                   else {"name": q.name, "kind": "tensor1-f32", "shape_symbol": q.shape_symbol}
+                   for q in b.program.params],
+        "kernel_count": 1,
+        "temporary_count": 0,
+        "generated_files": files,
+    }
+    if not p.uses_workspace:
+        d["no_workspace_symbol"] = p.symbol + "_noworkspace"
+    d["stream_symbol"] = p.symbol + "_stream"
+    if multi_gpu:
+        d["dist_symbol"] = p.symbol + "_dist"
+        d["dist_workspace_symbol"] = p.symbol + "_dist_workspace_size"
+        d["multi_symbol"] = p.symbol + "_multi"
+    d["b200_plan"] = plan_to_json(p)
+    return d
+
+
+def _manifest(mode, project_root, package, opts, artifact, header, source, entry_files,
+              commands) -> str:
+    obj = {
+        "mode": mode,
+        "target_backend": "cuda",
+        "backend": "loom-b200",
+        "project_root": project_root,
+        "package_name": package,
+        "artifact_kind": opts.kind,
+        "cuda_arch": CUDA_ARCH,
+        "cuda_platform": "b200",
+        "cuda_tuning": {"block_size": 256, "unroll_float4": 4, "tile_elements": 4096,
+                        "max_partials": 4096, "grid": "sm_count x resident CTAs per SM"},
+        "artifact_path": artifact,
+        "header_path": header,
+        "source_path": source,
+        "entries": [_entry_json(b, files, package, opts.multi_gpu) for b, files in entry_files],
+        "optimizations": opts.to_json(),
+        "build_commands": commands,
+    }
+    if opts.multi_gpu:
+        obj["comm_symbols"] = [line.split("(")[0].split()[-1]
+                               for line in codegen.comm_prototypes(package)]
+    return json.dumps(obj, indent=2)
+
+
+def _report(title, project_root, package, opts, artifact, header, source, bundles,
+            commands) -> str:
+    lines = [title, "",
+             f"- project root: `{project_root}`",
+             "- pipeline: `TensorIR -> B200 fused plan -> sm_100a CUDA`",
+             f"- package: `{package}`",
+             f"- artifact kind: `{opts.kind}`",
+             f"- CUDA arch: `{CUDA_ARCH}`",
+             f"- artifact: `{artifact}`",
+             f"- header: `{header}`",
+             f"- source: `{source}`",
+             f"- exported entrypoints: `{len(bundles)}`",
+             "- enabled optimizations: " + (", ".join(opts.enabled) if opts.enabled else "none"),
+             ""]
+    for b in bundles:
+        p = b.plan
+        lines += [f"## `{p.symbol}`", "",
+                  f"- entrypoint: `{b.program.entry_name}`",
+                  f"- source: `{b.source_file}`",
+                  f"- result kind: `{b.program.result_kind}`",
+                  f"- kernel: `{p.kind}`" + (f" ({p.reduce_kind})" if p.reduce_kind else ""),
+                  f"- launches per call: `{1 if p.kind == 'map' else 2}`",
+                  f"- fused nodes: `{len(p.fused_node_ids)}`",
+                  f"- HBM bytes per element: `{p.bytes_per_element}`",
+                  "- temporary allocations: `0`", ""]
+    lines += ["## Build Commands", ""] + [f"- `{c}`" for c in commands] + [""]
+    return "\n".join(lines)
+
+
+def _write(path: str, text: str) -> None:
+    os.makedirs(os.path.dirname(path), exist_ok=True)
+    with open(path, "w", encoding="utf-8") as fh:
+        fh.write(text)
+
+
+def _write_entry_dir(out_dir: str, b: EntryBundle) -> List[str]:
+    sym = b.plan.symbol
+    rel = os.path.join("entries", sym)
+    files = {
+        "tensor_ir.json": program_to_string(b.program),
+        "cuda_plan.json": json.dumps(plan_to_json(b.plan), indent=2),
+        "kernel_plan.json": json.dumps(plan_to_json(b.plan), indent=2),
+        "backend_analysis.json": json.dumps({
+            "entry_name": b.program.entry_name,
+            "hbm_bytes_per_element": b.plan.bytes_per_element,
+            "roofline": "hbm",
+            "tensor_slots": b.plan.slots,
+        }, indent=2),
+        "report.md": "\n".join([
+            "# Loom Entry Report", "",
+            f"- entrypoint: `{b.program.entry_name}`",
+            f"- module: `{b.module_name}`",
+            f"- source: `{b.source_file}`",
+            "- pipeline: `TensorIR -> B200 fused plan -> sm_100a CUDA`",
+            f"- exported symbol: `{sym}`",
+            f"- workspace function: `{b.plan.workspace_symbol}`",
+            f"- result kind: `{b.program.result_kind}`",
+            "- generated kernels: `1`",
+            "- temporary allocations: `0`", ""]),
+    }
+    out = []
+    for name, text in files.items():
+        _write(os.path.join(out_dir, rel, name), text)
+        out.append(os.path.join(rel, name))
+    return out
+
+
+@dataclass
+class PackageResult:
+    project_root: str
+    package_name: str
+    artifact_path: str
+    header_path: str
+    source_path: str
+    manifest_path: str
+    report_path: str
+    build_commands: List[str]
+
+
+def generate_package(project_root: str, out_dir: str, opts: Optional[Options] = None,
+                     module_filters: Sequence[str] = (), entry_filters: Sequence[str] = (),
+                     build: bool = True, package_name: Optional[str] = None) -> PackageResult:
+    """``loomc package --target cuda`` (cuda_backend.ml:2733-2816) for B200."""
+    opts = opts or Options()
+    project_root = os.path.abspath(project_root)
+    package = package_name or package_name_of_root(project_root)
+    bundles = discover_entries(project_root, module_filters, entry_filters)
+    if not bundles:
+        raise TensorIRError("no Loom entries matched the requested project selection")
+    symbols = [b.plan.symbol for b in bundles]
+    if len(set(symbols)) != len(symbols):
+        raise TensorIRError("duplicate entry symbols in project: " + ", ".join(symbols))
+    out_dir = os.path.abspath(out_dir)
+    include_root = os.path.join(out_dir, "include")
+    header = os.path.join(include_root, "loom", package + ".h")
+    source = os.path.join(out_dir, "src-gen", package + ".cu")
+    ext = "so" if opts.kind == "shared" else "a"
+    artifact = os.path.join(out_dir, f"lib{package}.{ext}")
+    plans = [b.plan for b in bundles]
+    _write(header, codegen.render_header(package, plans, opts.multi_gpu))
+    _write(source, codegen.render_source(package, f"loom/{package}.h", plans,
+                                         opts.async_return, opts.multi_gpu))
+    entry_files = [(b, _write_entry_dir(out_dir, b)) for b in bundles]
+    commands = build_artifact(opts, include_root, source, artifact) if build else \
+        [shlex.join(nvcc_command(opts, include_root, source, artifact))]
+    manifest = os.path.join(out_dir, "manifest.json")
+    report = os.path.join(out_dir, "report.md")
+    _write(manifest, _manifest("package", project_root, package, opts, artifact, header, source,
+                               entry_files, commands))
+    _write(report, _report("# Loom Package Report", project_root, package, opts, artifact,
+                           header, source, bundles, commands))
+    return PackageResult(project_root, package, artifact, header, source, manifest, report,
+                         commands)
+
+
+def compile_entry(source_file: str, entry_name: str, out_dir: str,
+                  opts: Optional[Options] = None, build: bool = True) -> PackageResult:
+    """``loomc compile <file> --entry e --target cuda`` (cuda_backend.ml:2675-2731)."""
+    opts = opts or Options()
+    module = module_name_of_file(source_file)
+    progs = [p for p in load_entries_file(source_file) if p.entry_name == entry_name]
+    if not progs:
+        raise TensorIRError(f"entry {entry_name!r} not found in {source_file}")
+    prog = progs[0]
+    b = EntryBundle(module, os.path.abspath(source_file), prog, plan_entry(prog, module))
+    out_dir = os.path.abspath(out_dir)
+    header = os.path.join(out_dir, f"{entry_name}_cuda.h")
+    source = os.path.join(out_dir, f"{entry_name}_cuda.cu")
+    artifact = os.path.join(out_dir, f"lib{entry_name}.so")
+    package = b.plan.symbol
+    _write(header, codegen.render_header(package, [b.plan], opts.multi_gpu))
+    _write(source, codegen.render_source(package, os.path.basename(header), [b.plan],
+                                         opts.async_return, opts.multi_gpu))
+    _write(os.path.join(out_dir, "tensor_ir.json"), program_to_string(prog))
+    _write(os.path.join(out_dir, "cuda_plan.json"), json.dumps(plan_to_json(b.plan), indent=2))
+    commands = build_artifact(opts, out_dir, source, artifact) if build else \
+        [shlex.join(nvcc_command(opts, out_dir, source, artifact))]
+    files = [os.path.basename(p) for p in (header, source, artifact)]
+    manifest = os.path.join(out_dir, "manifest.json")
+    report = os.path.join(out_dir, "report.md")
+    _write(manifest, _manifest("compile", os.path.dirname(b.source_file), package, opts,
+                               artifact, header, source, [(b, files)], commands))
+    _write(report, _report("# Loom CUDA Compile Report", os.path.dirname(b.source_file), package,
+                           opts, artifact, header, source, [b], commands))
+    return PackageResult(os.path.dirname(b.source_file), package, artifact, header, source,
+                         manifest, report, commands)

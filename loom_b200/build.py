@@ -1,0 +1,51 @@
+"""In-tree build of the shipped benchmark-suite package.
+
+``build_suite()`` packages ``loom_b200/suite`` (the five workload
+configurations of the hot path, module ``kernels``) into
+``loom_b200/_built/b200_suite/`` with the reference's default flags (so the
+plain entry points synchronise like the reference's); ``load_suite()`` loads
+it.  The built ``.so`` stays in the tree so that it travels with the
+repository to the GPU machine.
+"""
+
+from __future__ import annotations
+
+import os
+
+from . import artifact
+from .loader import Package
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SUITE_PROJECT = os.path.join(HERE, "suite")
+BUILT_DIR = os.path.join(HERE, "_built")
+SUITE_DIR = os.path.join(BUILT_DIR, "b200_suite")
+
+
+def _newest_source_mtime() -> float:
+    newest = 0.0
+    for root in (SUITE_PROJECT, os.path.join(HERE, "csrc")):
+        for name in os.listdir(root):
+            newest = max(newest, os.path.getmtime(os.path.join(root, name)))
+    for name in ("codegen.py", "plan.py", "render.py", "artifact.py", "tensor_ir.py"):
+        newest = max(newest, os.path.getmtime(os.path.join(HERE, name)))
+    return newest
+
+
+def suite_is_current() -> bool:
+    lib = os.path.join(SUITE_DIR, "libb200_suite.so")
+    return os.path.exists(lib) and os.path.getmtime(lib) >= _newest_source_mtime()
+
+
+def build_suite(force: bool = False) -> artifact.PackageResult:
+    if not force and suite_is_current():
+        return None
+    return artifact.generate_package(SUITE_PROJECT, SUITE_DIR, artifact.Options())
+
+
+def load_suite() -> Package:
+    lib = os.path.join(SUITE_DIR, "libb200_suite.so")
+    if not os.path.exists(lib):
+        raise FileNotFoundError(
+            f"{lib} is missing: build it with `python -c 'import loom_b200.build as b; "
+            "b.build_suite()'` (needs nvcc)")
+    return Package(SUITE_DIR)

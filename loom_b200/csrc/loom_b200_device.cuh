@@ -1,0 +1,336 @@
+// loom_b200_device.cuh -- hand-written sm_100a kernels behind every generated
+// Loom entry point.
+//
+// Every Loom entry lowers to ONE streaming kernel (plus, for reductions, a
+// one-CTA finalize).  The generated code only supplies a body functor: a
+// struct with `static constexpr int kInputs` and
+// `__device__ float operator()(const float* in) const`, which evaluates the
+// whole fused element-wise DAG of the entry for one element from the values
+// of its kInputs distinct tensor parameters.  Intermediates of a fused chain
+// live in registers and never reach HBM.
+//
+// These kernels replace the reference's emitted templates
+// (src/loom_backend_cuda/cuda_backend.ml:908-1627): the grid-stride scalar and
+// float4 element-wise kernels, the first-stage reduction with its
+// shared-memory or shuffle block reduce, and the multi-launch combine tree.
+//
+// Layout and strategy (B200):
+//  * all tensors are 1D contiguous fp32 in HBM; when every pointer of a call
+//    has the same address mod 16 the kernel peels a head of 0..3 elements,
+//    streams the body as 128-bit float4 loads/stores (ld.global.cs /
+//    st.global.cs: each byte is touched once, so it is marked evict-first)
+//    and finishes a tail of 0..3 elements; otherwise it streams 32-bit
+//    elements;
+//  * persistent grid of (SM count x resident CTAs per SM) CTAs, each CTA
+//    walks tiles of kThreads*kUnroll float4 per input with a grid stride,
+//    issuing kUnroll independent 16-byte loads per input per thread before
+//    using any of them (memory-level parallelism for HBM3e latency);
+//  * reductions: sums accumulate each thread's tile chunk (16 values) in
+//    fp32 and fold the chunk into an fp64 per-thread accumulator; CTAs reduce
+//    with xor-shuffle butterflies and write one fp64 partial each to the
+//    caller's workspace; the finalize CTA sums the partials in a fixed order.
+//    No float atomics anywhere: the result is bit-reproducible for a given
+//    grid.  Max keeps fp32 fmaxf throughout (exact in any order).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+namespace loomb {
+
+constexpr int kThreads = 256;                                 // threads per CTA
+constexpr int kUnroll = 4;                                    // float4 per input per thread per tile
+constexpr int64_t kTileVecs = (int64_t)kThreads * kUnroll;    // float4 per input per CTA tile
+constexpr int64_t kTileElems = kTileVecs * 4;                 // 4096 floats per input per tile
+constexpr int kMaxPartials = 4096;                            // upper bound on reduction CTAs
+constexpr int kMaxDevices = 64;
+
+template <int K>
+struct Ptrs {
+  const float* p[K];
+};
+
+// ---------------------------------------------------------------------------
+// streaming memory access
+
+__device__ __forceinline__ float4 load_stream(const float4* p) { return __ldcs(p); }
+__device__ __forceinline__ float load_stream(const float* p) { return __ldcs(p); }
+__device__ __forceinline__ void store_stream(float4* p, const float4& v) { __stcs(p, v); }
+__device__ __forceinline__ void store_stream(float* p, float v) { __stcs(p, v); }
+
+template <class Body>
+__device__ __forceinline__ float4 apply4(const Body& body, const float4 (&v)[Body::kInputs]) {
+  constexpr int K = Body::kInputs;
+  float a[K];
+  float4 r;
+#pragma unroll
+  for (int k = 0; k < K; ++k) a[k] = v[k].x;
+  r.x = body(a);
+#pragma unroll
+  for (int k = 0; k < K; ++k) a[k] = v[k].y;
+  r.y = body(a);
+#pragma unroll
+  for (int k = 0; k < K; ++k) a[k] = v[k].z;
+  r.z = body(a);
+#pragma unroll
+  for (int k = 0; k < K; ++k) a[k] = v[k].w;
+  r.w = body(a);
+  return r;
+}
+
+template <class Body>
+__device__ __forceinline__ float apply1(const Body& body, const Ptrs<Body::kInputs>& in, int64_t i) {
+  constexpr int K = Body::kInputs;
+  float a[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) a[k] = load_stream(in.p[k] + i);
+  return body(a);
+}
+
+// ---------------------------------------------------------------------------
+// element-wise map: out[i] = body(in_0[i], ..., in_{K-1}[i])
+
+// Vector path.  Preconditions (checked by the host launcher): every pointer
+// is 4-byte aligned and congruent to `out` mod 16; head = number of leading
+// elements before the first 16-byte boundary (0..3, at most n).
+template <class Body>
+__global__ void __launch_bounds__(kThreads)
+map_vec_kernel(float* __restrict__ out, const Ptrs<Body::kInputs> in, const int64_t n,
+               const int64_t head, const Body body) {
+  constexpr int K = Body::kInputs;
+  const int64_t nvec = (n - head) >> 2;
+  const float4* src[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) src[k] = reinterpret_cast<const float4*>(in.p[k] + head);
+  float4* dst = reinterpret_cast<float4*>(out + head);
+  const int64_t stride = (int64_t)gridDim.x * kTileVecs;
+  for (int64_t t = (int64_t)blockIdx.x * kTileVecs; t < nvec; t += stride) {
+    const int64_t i0 = t + threadIdx.x;
+    if (t + kTileVecs <= nvec) {
+      float4 v[kUnroll][K];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+        for (int k = 0; k < K; ++k) v[u][k] = load_stream(src[k] + i0 + u * kThreads);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) store_stream(dst + i0 + u * kThreads, apply4(body, v[u]));
+    } else {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t i = i0 + u * kThreads;
+        if (i < nvec) {
+          float4 v[K];
+#pragma unroll
+          for (int k = 0; k < K; ++k) v[k] = load_stream(src[k] + i);
+          store_stream(dst + i, apply4(body, v));
+        }
+      }
+    }
+  }
+  // Ragged edges: threads 0..2 take the head, threads 4..6 the tail (both <= 3).
+  if (blockIdx.x == gridDim.x - 1) {
+    const int64_t tail0 = head + (nvec << 2);
+    const int r = threadIdx.x;
+    int64_t i = -1;
+    if (r < head) i = r;
+    else if (r >= 4 && (int64_t)(r - 4) < n - tail0) i = tail0 + (r - 4);
+    if (i >= 0) store_stream(out + i, apply1(body, in, i));
+  }
+}
+
+// Scalar path for calls whose pointers disagree mod 16.
+template <class Body>
+__global__ void __launch_bounds__(kThreads)
+map_scalar_kernel(float* __restrict__ out, const Ptrs<Body::kInputs> in, const int64_t n,
+                  const Body body) {
+  constexpr int64_t kTile = (int64_t)kThreads * kUnroll * 4;
+  const int64_t stride = (int64_t)gridDim.x * kTile;
+  for (int64_t t = (int64_t)blockIdx.x * kTile; t < n; t += stride) {
+    constexpr int kU = kUnroll * 4;
+    if (t + kTile <= n) {
+      float v[kU][Body::kInputs];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+#pragma unroll
+        for (int k = 0; k < Body::kInputs; ++k)
+          v[u][k] = load_stream(in.p[k] + t + u * kThreads + threadIdx.x);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) store_stream(out + t + u * kThreads + threadIdx.x, body(v[u]));
+    } else {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = t + u * kThreads + threadIdx.x;
+        if (i < n) store_stream(out + i, apply1(body, in, i));
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// reductions
+
+struct SumOp {
+  using Acc = double;
+  static __device__ __forceinline__ double init() { return 0.0; }
+  static __device__ __forceinline__ float chunk4(const float4& v) {
+    return __fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w));
+  }
+  static __device__ __forceinline__ float chunk2(float a, float b) { return __fadd_rn(a, b); }
+  static __device__ __forceinline__ double absorb(double acc, float chunk) {
+    return __dadd_rn(acc, (double)chunk);
+  }
+  static __device__ __forceinline__ double combine(double a, double b) { return __dadd_rn(a, b); }
+  static __device__ __forceinline__ float to_float(double a) { return __double2float_rn(a); }
+};
+
+struct MaxOp {
+  using Acc = float;
+  static __device__ __forceinline__ float init() { return -INFINITY; }
+  static __device__ __forceinline__ float chunk4(const float4& v) {
+    return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+  }
+  static __device__ __forceinline__ float chunk2(float a, float b) { return fmaxf(a, b); }
+  static __device__ __forceinline__ float absorb(float acc, float chunk) { return fmaxf(acc, chunk); }
+  static __device__ __forceinline__ float combine(float a, float b) { return fmaxf(a, b); }
+  static __device__ __forceinline__ float to_float(float a) { return a; }
+};
+
+// Deterministic CTA reduce: xor butterflies inside each warp, then warp 0
+// folds the per-warp values in warp order.  The result is valid in thread 0.
+template <class Op>
+__device__ __forceinline__ typename Op::Acc block_reduce(typename Op::Acc v) {
+  using Acc = typename Op::Acc;
+  __shared__ Acc warp_vals[kThreads / 32];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v = Op::combine(v, __shfl_xor_sync(0xffffffffu, v, off));
+  if (lane == 0) warp_vals[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < (kThreads / 32) ? warp_vals[lane] : Op::init();
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = Op::combine(v, __shfl_xor_sync(0xffffffffu, v, off));
+  }
+  return v;
+}
+
+template <class Op, class Body>
+__global__ void __launch_bounds__(kThreads)
+reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInputs> in,
+                  const int64_t n, const int64_t head, const Body body) {
+  constexpr int K = Body::kInputs;
+  using Acc = typename Op::Acc;
+  const int64_t nvec = (n - head) >> 2;
+  const float4* src[K];
+#pragma unroll
+  for (int k = 0; k < K; ++k) src[k] = reinterpret_cast<const float4*>(in.p[k] + head);
+  Acc acc = Op::init();
+  const int64_t stride = (int64_t)gridDim.x * kTileVecs;
+  for (int64_t t = (int64_t)blockIdx.x * kTileVecs; t < nvec; t += stride) {
+    const int64_t i0 = t + threadIdx.x;
+    if (t + kTileVecs <= nvec) {
+      float4 v[kUnroll][K];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+        for (int k = 0; k < K; ++k) v[u][k] = load_stream(src[k] + i0 + u * kThreads);
+      float c[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) c[u] = Op::chunk4(apply4(body, v[u]));
+      acc = Op::absorb(acc, Op::chunk2(Op::chunk2(c[0], c[1]), Op::chunk2(c[2], c[3])));
+    } else {
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int64_t i = i0 + u * kThreads;
+        if (i < nvec) {
+          float4 v[K];
+#pragma unroll
+          for (int k = 0; k < K; ++k) v[k] = load_stream(src[k] + i);
+          acc = Op::absorb(acc, Op::chunk4(apply4(body, v)));
+        }
+      }
+    }
+  }
+  if (blockIdx.x == gridDim.x - 1) {
+    const int64_t tail0 = head + (nvec << 2);
+    const int r = threadIdx.x;
+    int64_t i = -1;
+    if (r < head) i = r;
+    else if (r >= 4 && (int64_t)(r - 4) < n - tail0) i = tail0 + (r - 4);
+    if (i >= 0) acc = Op::absorb(acc, apply1(body, in, i));
+  }
+  acc = block_reduce<Op>(acc);
+  if (threadIdx.x == 0) partials[blockIdx.x] = acc;
+}
+
+template <class Op, class Body>
+__global__ void __launch_bounds__(kThreads)
+reduce_scalar_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInputs> in,
+                     const int64_t n, const Body body) {
+  using Acc = typename Op::Acc;
+  constexpr int kU = kUnroll * 4;
+  constexpr int64_t kTile = (int64_t)kThreads * kU;
+  const int64_t stride = (int64_t)gridDim.x * kTile;
+  Acc acc = Op::init();
+  for (int64_t t = (int64_t)blockIdx.x * kTile; t < n; t += stride) {
+    if (t + kTile <= n) {
+      float v[kU][Body::kInputs];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+#pragma unroll
+        for (int k = 0; k < Body::kInputs; ++k)
+          v[u][k] = load_stream(in.p[k] + t + u * kThreads + threadIdx.x);
+      float c[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float4 f;
+        f.x = body(v[4 * q + 0]);
+        f.y = body(v[4 * q + 1]);
+        f.z = body(v[4 * q + 2]);
+        f.w = body(v[4 * q + 3]);
+        c[q] = Op::chunk4(f);
+      }
+      acc = Op::absorb(acc, Op::chunk2(Op::chunk2(c[0], c[1]), Op::chunk2(c[2], c[3])));
+    } else {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = t + u * kThreads + threadIdx.x;
+        if (i < n) acc = Op::absorb(acc, apply1(body, in, i));
+      }
+    }
+  }
+  acc = block_reduce<Op>(acc);
+  if (threadIdx.x == 0) partials[blockIdx.x] = acc;
+}
+
+// One CTA folds `count` CTA partials in a fixed order.  Writes the fp32
+// result to `out` (if non-null) and the full-precision value to
+// `partial_out` (if non-null; the multi-GPU path all-gathers it).
+template <class Op>
+__global__ void __launch_bounds__(kThreads)
+reduce_finalize_kernel(const typename Op::Acc* __restrict__ partials, const int count,
+                       float* __restrict__ out, typename Op::Acc* __restrict__ partial_out) {
+  using Acc = typename Op::Acc;
+  Acc acc = Op::init();
+  for (int i = threadIdx.x; i < count; i += kThreads) acc = Op::combine(acc, partials[i]);
+  acc = block_reduce<Op>(acc);
+  if (threadIdx.x == 0) {
+    if (out != nullptr) out[0] = Op::to_float(acc);
+    if (partial_out != nullptr) partial_out[0] = acc;
+  }
+}
+
+// Folds `count` per-rank values (gathered in rank order) into out[0].
+template <class Op>
+__global__ void rank_combine_kernel(const typename Op::Acc* __restrict__ ranks, const int count,
+                                    float* __restrict__ out) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) {
+    typename Op::Acc acc = Op::init();
+    for (int r = 0; r < count; ++r) acc = Op::combine(acc, ranks[r]);
+    out[0] = Op::to_float(acc);
+  }
+}
+
+}  // namespace loomb

@@ -1,0 +1,255 @@
+"""Thin ctypes / PyTorch host loader over a generated package's C ABI.
+
+Mirrors the reference harness's CUDA runner
+(``experiments/source/harness/run.py:1795-1895``): read ``manifest.json``,
+``ctypes.CDLL`` the artefact, bind each entry from its manifest ``params``,
+size and cache the workspace with ``<symbol>_workspace_size``, and call with
+device pointers.  A non-zero status raises ``LoomError``.
+
+There is no CPU fallback: if the library cannot be loaded, or a tensor is not
+a contiguous float32 CUDA tensor, the call fails.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+from typing import Dict, List, Optional, Sequence
+
+STATUS_NAMES = {0: "OK", 1: "INVALID_ARGUMENT", 2: "WORKSPACE_TOO_SMALL", 3: "CUDA_ERROR",
+                4: "COMM_ERROR"}
+
+
+class LoomError(RuntimeError):
+    def __init__(self, symbol: str, status: int):
+        super().__init__(f"{symbol} returned {status} ({STATUS_NAMES.get(status, '?')})")
+        self.status = status
+
+
+def _torch():
+    import torch
+    return torch
+
+
+class Entry:
+    """One exported entry of a package."""
+
+    def __init__(self, lib: ctypes.CDLL, meta: dict, package: "Package"):
+        self.lib = lib
+        self.meta = meta
+        self.package = package
+        self.name = meta["entry_name"]
+        self.symbol = meta["symbol_name"]
+        self.params = meta["params"]
+        self.result_kind = meta["result_kind"]
+        self.tensor_params = [p["name"] for p in self.params if p["kind"] == "tensor1-f32"]
+        self.scalar_params = [p["name"] for p in self.params if p["kind"] == "scalar-f32"]
+        ptypes = [ctypes.c_float if p["kind"] == "scalar-f32" else ctypes.c_void_p
+                  for p in self.params]
+        self.fn = getattr(lib, self.symbol)
+        self.fn.argtypes = ptypes + [ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                     ctypes.c_size_t]
+        self.fn.restype = ctypes.c_int
+        self.ws_fn = getattr(lib, meta["workspace_symbol"])
+        self.ws_fn.argtypes = [ctypes.c_int64]
+        self.ws_fn.restype = ctypes.c_size_t
+        self.stream_fn = getattr(lib, meta.get("stream_symbol", self.symbol + "_stream"))
+        self.stream_fn.argtypes = list(self.fn.argtypes) + [ctypes.c_void_p]
+        self.stream_fn.restype = ctypes.c_int
+        self.noworkspace_fn = None
+        if meta.get("no_workspace_symbol"):
+            self.noworkspace_fn = getattr(lib, meta["no_workspace_symbol"])
+            self.noworkspace_fn.argtypes = ptypes + [ctypes.c_int64, ctypes.c_void_p]
+            self.noworkspace_fn.restype = ctypes.c_int
+        self.dist_fn = None
+        if meta.get("dist_symbol"):
+            self.dist_fn = getattr(lib, meta["dist_symbol"])
+            self.dist_fn.argtypes = ptypes + [ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                                              ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
+            self.dist_fn.restype = ctypes.c_int
+            self.dist_ws_fn = getattr(lib, meta["dist_workspace_symbol"])
+            self.dist_ws_fn.argtypes = [ctypes.c_int64]
+            self.dist_ws_fn.restype = ctypes.c_size_t
+        self._ws: Dict[tuple, object] = {}
+
+    # -- helpers ------------------------------------------------------------
+    def workspace_size(self, n: int) -> int:
+        return int(self.ws_fn(int(n)))
+
+    def workspace(self, n: int, device=None, dist: bool = False):
+        """Cached device workspace for n elements (None when not needed)."""
+        torch = _torch()
+        size = int(self.dist_ws_fn(n)) if dist else self.workspace_size(n)
+        if size <= 0:
+            return None
+        device = torch.device(device if device is not None else "cuda")
+        key = (str(device), size)
+        ws = self._ws.get(key)
+        if ws is None:
+            ws = torch.empty(size, dtype=torch.uint8, device=device)
+            self._ws[key] = ws
+        return ws
+
+    def _args(self, inputs: Dict[str, object], n: Optional[int] = None) -> List[object]:
+        torch = _torch()
+        args: List[object] = []
+        for p in self.params:
+            v = inputs[p["name"]]
+            if p["kind"] == "scalar-f32":
+                args.append(ctypes.c_float(float(v)))
+            else:
+                if not (isinstance(v, torch.Tensor) and v.is_cuda and v.dtype == torch.float32
+                        and v.is_contiguous()):
+                    raise TypeError(f"{self.name}: {p['name']} must be a contiguous float32 "
+                                    "CUDA tensor")
+                if n is not None and v.numel() != n:
+                    raise ValueError(f"{self.name}: {p['name']} has {v.numel()} elements, "
+                                     f"expected {n}")
+                args.append(ctypes.c_void_p(v.data_ptr()))
+        return args
+
+    def _n(self, inputs: Dict[str, object]) -> int:
+        return int(inputs[self.tensor_params[0]].numel())
+
+    def new_output(self, n: int, device):
+        torch = _torch()
+        if self.result_kind == "tensor":
+            return torch.empty(n, dtype=torch.float32, device=device)
+        return torch.empty(1, dtype=torch.float32, device=device)
+
+    # -- calls ----------------------------------------------------------------
+    def __call__(self, out=None, stream=None, **inputs):
+        """Run on device tensors; returns the output tensor (n floats, or 1
+        float for a scalar result).  With `stream` (a torch.cuda.Stream or a
+        raw handle) the call is asynchronous on that stream."""
+        n = self._n(inputs)
+        device = inputs[self.tensor_params[0]].device
+        if out is None:
+            out = self.new_output(n, device)
+        args = self._args(inputs, n)
+        ws = self.workspace(n, device)
+        wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
+        wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
+        tail = [ctypes.c_int64(n), ctypes.c_void_p(out.data_ptr()), wsp, wss]
+        if stream is None:
+            status = self.fn(*args, *tail)
+        else:
+            handle = getattr(stream, "cuda_stream", stream)
+            status = self.stream_fn(*args, *tail, ctypes.c_void_p(handle))
+        if status != 0:
+            raise LoomError(self.symbol, status)
+        return out
+
+    def call_raw(self, *args) -> int:
+        return int(self.fn(*args))
+
+    def dist(self, comm: "Comm", out=None, stream=None, **inputs):
+        """This rank's shard of a multi-GPU call (one process per GPU)."""
+        if self.dist_fn is None:
+            raise RuntimeError(f"{self.package.name} was built without multi-GPU entries")
+        n = self._n(inputs)
+        device = inputs[self.tensor_params[0]].device
+        if out is None:
+            out = self.new_output(n, device)
+        args = self._args(inputs, n)
+        ws = self.workspace(n, device, dist=True)
+        wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
+        wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
+        handle = getattr(stream, "cuda_stream", stream) if stream is not None else None
+        status = self.dist_fn(*args, ctypes.c_int64(n), ctypes.c_void_p(out.data_ptr()), wsp,
+                              wss, ctypes.c_void_p(comm.handle), ctypes.c_void_p(handle))
+        if status != 0:
+            raise LoomError(self.symbol + "_dist", status)
+        return out
+
+
+class Comm:
+    """An NCCL communicator owned by a package (one rank of one process)."""
+
+    def __init__(self, package: "Package", handle: int, nranks: int, rank: int):
+        self.package = package
+        self.handle = handle
+        self.nranks = nranks
+        self.rank = rank
+
+    def destroy(self) -> None:
+        if self.handle:
+            self.package._comm_destroy(ctypes.c_void_p(self.handle))
+            self.handle = 0
+
+
+class Package:
+    """A built package: ``Package(out_dir)`` or ``Package(manifest_path)``."""
+
+    def __init__(self, path: str):
+        manifest = path if path.endswith(".json") else os.path.join(path, "manifest.json")
+        with open(manifest, "r", encoding="utf-8") as fh:
+            self.manifest = json.load(fh)
+        self.name = self.manifest["package_name"]
+        artifact = self.manifest["artifact_path"]
+        if not os.path.exists(artifact):
+            artifact = os.path.join(os.path.dirname(manifest), os.path.basename(artifact))
+        self.path = artifact
+        self.lib = ctypes.CDLL(artifact)
+        self.entries = {e["entry_name"]: Entry(self.lib, e, self)
+                        for e in self.manifest["entries"]}
+        prefix = f"loom_{self.name}_comm"
+        self._has_comm = hasattr(self.lib, prefix + "_unique_id")
+        if self._has_comm:
+            self._comm_id_size = getattr(self.lib, prefix + "_id_size")
+            self._comm_id_size.restype = ctypes.c_int
+            self._comm_unique_id = getattr(self.lib, prefix + "_unique_id")
+            self._comm_unique_id.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
+            self._comm_init_rank = getattr(self.lib, prefix + "_init_rank")
+            self._comm_init_rank.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+                                             ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t]
+            self._comm_init_all = getattr(self.lib, prefix + "_init_all")
+            self._comm_init_all.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+                                            ctypes.POINTER(ctypes.c_int)]
+            self._comm_destroy = getattr(self.lib, prefix + "_destroy")
+            self._comm_destroy.argtypes = [ctypes.c_void_p]
+
+    def __getitem__(self, entry: str) -> Entry:
+        return self.entries[entry]
+
+    def __getattr__(self, entry: str) -> Entry:
+        entries = self.__dict__.get("entries", {})
+        if entry in entries:
+            return entries[entry]
+        raise AttributeError(entry)
+
+    # -- communicators ------------------------------------------------------
+    def comm_unique_id(self) -> bytes:
+        size = int(self._comm_id_size())
+        buf = ctypes.create_string_buffer(size)
+        status = self._comm_unique_id(buf, size)
+        if status != 0:
+            raise LoomError("comm_unique_id", status)
+        return buf.raw
+
+    def comm_init_rank(self, nranks: int, rank: int, uid: bytes) -> Comm:
+        """One rank of a communicator on the current CUDA device (collective)."""
+        handle = ctypes.c_void_p(0)
+        buf = ctypes.create_string_buffer(uid, len(uid))
+        status = self._comm_init_rank(ctypes.byref(handle), nranks, rank, buf, len(uid))
+        if status != 0:
+            raise LoomError("comm_init_rank", status)
+        return Comm(self, handle.value, nranks, rank)
+
+    def comm_from_process_group(self, group=None) -> Comm:
+        """Rendezvous a communicator over an initialised torch.distributed group."""
+        import torch.distributed as dist
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        box = [self.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0, group=group)
+        return self.comm_init_rank(world, rank, box[0])
+
+    def comm_init_all(self, devices: Sequence[int]) -> List[Comm]:
+        n = len(devices)
+        handles = (ctypes.c_void_p * n)()
+        devs = (ctypes.c_int * n)(*devices)
+        status = self._comm_init_all(handles, n, devs)
+        if status != 0:
+            raise LoomError("comm_init_all", status)
+        return [Comm(self, handles[i], n, i) for i in range(n)]

@@ -1,0 +1,60 @@
+"""Regenerate the golden fixtures under tests/golden/ from the reference.
+
+Run in a checkout that has the reference mounted (it is read-only data here;
+nothing at test time reads it):
+
+    python tests/golden/make_golden.py /path/to/reference
+
+* ``reference_ir/``: the reference's own golden IR files
+  (``test/golden/saxpy_loom_lambda.json``, ``test/golden/l2_norm_sq_tensor_ir.json``),
+  copied verbatim;
+* ``front_ir/<module>.<entry>.json``: FrontIR that the reference's Python
+  frontend (``src/frontends/python/loom_frontend_python.py front-ir-json``)
+  prints for the suite entries and for the reference's Python examples and
+  package fixture.
+"""
+
+import json
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+
+
+def main(ref: str) -> None:
+    out_ir = os.path.join(HERE, "reference_ir")
+    os.makedirs(out_ir, exist_ok=True)
+    for name in ("saxpy_loom_lambda.json", "l2_norm_sq_tensor_ir.json"):
+        shutil.copyfile(os.path.join(ref, "test", "golden", name), os.path.join(out_ir, name))
+    frontend = os.path.join(ref, "src", "frontends", "python", "loom_frontend_python.py")
+    sources = {
+        os.path.join(ROOT, "loom_b200", "suite", "kernels.py"):
+            ["saxpy", "relu", "dot", "l2_norm_sq", "max_value", "affine_relu", "pipeline_sum"],
+        os.path.join(ref, "examples", "saxpy.py"): ["saxpy"],
+        os.path.join(ref, "examples", "relu.py"): ["relu"],
+        os.path.join(ref, "examples", "dot.py"): ["dot"],
+        os.path.join(ref, "examples", "l2_norm_sq.py"): ["l2_norm_sq"],
+        os.path.join(ref, "experiments", "source", "python", "dot_pipeline.py"): ["dot_pipeline"],
+        os.path.join(ref, "test", "fixtures", "python_package_project", "kernels.py"):
+            ["saxpy", "relu", "dot"],
+    }
+    out_front = os.path.join(HERE, "front_ir")
+    os.makedirs(out_front, exist_ok=True)
+    for path, entries in sources.items():
+        tag = os.path.basename(os.path.dirname(path)) + "_" + os.path.splitext(
+            os.path.basename(path))[0]
+        for entry in entries:
+            proc = subprocess.run([sys.executable, frontend, "front-ir-json", path, "--entry", entry],
+                                  capture_output=True, text=True, check=True)
+            obj = json.loads(proc.stdout)
+            with open(os.path.join(out_front, f"{tag}.{entry}.json"), "w") as fh:
+                json.dump(obj, fh, indent=1, sort_keys=True)
+                fh.write("\n")
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

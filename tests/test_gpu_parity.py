@@ -1,0 +1,182 @@
+"""CUDA path vs the CPU oracle, through the C ABI, on seeded inputs.
+
+Bar (what a result must meet to pass):
+  * maps (saxpy, relu, affine_relu) and max_value: bit-exact (NaN only has to
+    be NaN);
+  * sums (dot, l2_norm_sq, pipeline_sum): |gpu - ref| <= 1e-6 * max(1, log2 n)
+    * max(|ref|, sqrt(sum v_i^2)), ref = the oracle's fp64 sum of the fp32
+    per-element values v_i.  For random data sqrt(sum v_i^2) is the natural
+    size of the sum, so this is the stated 1e-6*log2(N) relative bound; the
+    second term only matters when the sum cancels far below that size.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from loom_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+MAPS = ["saxpy", "relu", "affine_relu"]
+SUMS = ["dot", "l2_norm_sq", "pipeline_sum"]
+ALL = MAPS + SUMS + ["max_value"]
+SIZES = [1, 2, 3, 4, 5, 7, 8, 15, 16, 17, 255, 1023, 4096, 4099, 65541, 1 << 20, (1 << 20) + 3]
+
+
+def to_device(arr: np.ndarray, offset: int = 0) -> torch.Tensor:
+    """Copy into a fresh 256-byte aligned buffer starting `offset` floats in."""
+    buf = torch.empty(arr.shape[0] + 8, dtype=torch.float32, device="cuda")
+    view = buf[offset:offset + arr.shape[0]]
+    view.copy_(torch.from_numpy(arr))
+    return view
+
+
+def sum_scale(entry, inp):
+    if entry == "dot":
+        v = inp["x"].astype(np.float64) * inp["y"]
+    elif entry == "l2_norm_sq":
+        v = inp["x"].astype(np.float64) ** 2
+    else:
+        z = np.maximum(0.75 * inp["x"].astype(np.float64) + inp["y"], 0.0)
+        v = z * inp["w"]
+    return math.sqrt(float(np.sum(v * v)))
+
+
+def check_sum(entry, got, ref, inp, n):
+    tol = 1e-6 * max(1.0, math.log2(n)) * max(abs(ref), sum_scale(entry, inp))
+    assert abs(got - ref) <= tol, (entry, n, got, ref, tol)
+
+
+def run_entry(pkg, entry, inp, offsets=None):
+    e = pkg[entry]
+    offsets = offsets or {}
+    dev = {}
+    for k, v in inp.items():
+        dev[k] = to_device(v, offsets.get(k, 0)) if isinstance(v, np.ndarray) else v
+    n = next(v.shape[0] for v in inp.values() if isinstance(v, np.ndarray))
+    out = None
+    if e.result_kind == "tensor":
+        out = to_device(np.zeros(n, np.float32), offsets.get("out", 0))
+    res = e(out=out, **dev)
+    torch.cuda.synchronize()
+    return res.cpu().numpy()
+
+
+def assert_bits(got, ref):
+    nan = np.isnan(ref)
+    assert np.array_equal(np.isnan(got), nan)
+    assert np.array_equal(got[~nan].view(np.uint32), ref[~nan].view(np.uint32))
+
+
+@pytest.mark.parametrize("entry", ALL)
+@pytest.mark.parametrize("n", SIZES)
+def test_parity_sizes(suite_pkg, oracle, entry, n):
+    inp = workloads.entry_inputs(entry, n, seed_offset=n)
+    ref = oracle.run(entry, inp)
+    got = run_entry(suite_pkg, entry, inp)
+    if entry in MAPS:
+        assert_bits(got, ref)
+    elif entry == "max_value":
+        assert got[0] == np.float32(ref)
+    else:
+        check_sum(entry, float(got[0]), ref, inp, n)
+
+
+@pytest.mark.parametrize("entry", ALL)
+@pytest.mark.parametrize("offset", [1, 2, 3])
+def test_parity_misaligned_congruent(suite_pkg, oracle, entry, offset):
+    n = (1 << 16) + 11
+    inp = workloads.entry_inputs(entry, n, seed_offset=offset)
+    offs = {k: offset for k in list(inp) + ["out"]}
+    ref = oracle.run(entry, inp)
+    got = run_entry(suite_pkg, entry, inp, offs)
+    if entry in MAPS:
+        assert_bits(got, ref)
+    elif entry == "max_value":
+        assert got[0] == np.float32(ref)
+    else:
+        check_sum(entry, float(got[0]), ref, inp, n)
+
+
+@pytest.mark.parametrize("entry", ["saxpy", "affine_relu", "dot", "pipeline_sum"])
+def test_parity_non_congruent_pointers(suite_pkg, oracle, entry):
+    n = (1 << 15) + 5
+    inp = workloads.entry_inputs(entry, n, seed_offset=3)
+    offs = {"x": 1, "y": 2, "w": 3, "out": 0}
+    ref = oracle.run(entry, inp)
+    got = run_entry(suite_pkg, entry, inp, offs)
+    if entry in MAPS:
+        assert_bits(got, ref)
+    else:
+        check_sum(entry, float(got[0]), ref, inp, n)
+
+
+SPECIAL = np.float32([0.0, -0.0, 1e-45, -1e-45, 1.1754942e-38, -1.1754942e-38, np.inf, -np.inf,
+                      np.nan, 1.0, -1.0, 3.4028235e38, -3.4028235e38, 0.5, -0.5, 2.0 ** -126])
+
+
+@pytest.mark.parametrize("entry", ALL)
+def test_special_values(suite_pkg, oracle, entry):
+    rng = np.random.default_rng(7)
+    n = 4096 + 3
+    tensors, scalars, _ = workloads.ENTRY_SPECS[entry]
+    inp = {t: rng.choice(SPECIAL, size=n).astype(np.float32) for t in tensors}
+    inp.update(dict(scalars))
+    ref = oracle.run(entry, inp)
+    got = run_entry(suite_pkg, entry, inp)
+    if entry in MAPS:
+        assert_bits(got, ref)
+    elif entry == "max_value":
+        assert got[0] == np.float32(ref)
+    else:
+        # with inf/nan/FLT_MAX in play the sum is inf or nan on both sides
+        g, r = float(got[0]), ref
+        assert (math.isnan(g) and math.isnan(r)) or g == r or (
+            math.isfinite(r) and abs(g - r) <= 1e-6 * abs(r))
+
+
+def test_signed_zero_and_nan_max(suite_pkg, oracle):
+    for arr in (np.float32([-0.0, 0.0, -0.0, -0.0]), np.float32([-0.0] * 37),
+                np.float32([np.nan, -3.0, np.nan]), np.float32([np.nan] * 9)):
+        ref = oracle.run("max_value", {"x": arr})
+        got = run_entry(suite_pkg, "max_value", {"x": arr})[0]
+        assert got == np.float32(ref) or (np.isinf(ref) and np.isinf(got))
+        assert math.copysign(1.0, float(got)) == math.copysign(1.0, ref)
+    relu = run_entry(suite_pkg, "relu", {"x": np.float32([-0.0] * 11)})
+    assert np.all(relu.view(np.uint32) == 0)  # +0.0, as the oracle (and x>0?x:0) give
+
+
+def test_reductions_are_deterministic(suite_pkg):
+    inp = workloads.entry_inputs("dot", (1 << 22) + 1)
+    a = run_entry(suite_pkg, "dot", inp)
+    b = run_entry(suite_pkg, "dot", inp)
+    assert a.view(np.uint32)[0] == b.view(np.uint32)[0]
+
+
+def test_stream_entry_matches(suite_pkg, oracle):
+    inp = workloads.entry_inputs("pipeline_sum", 1 << 20)
+    ref = oracle.run("pipeline_sum", inp)
+    dev = {k: (torch.from_numpy(v).cuda() if isinstance(v, np.ndarray) else v)
+           for k, v in inp.items()}
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        out = suite_pkg["pipeline_sum"](stream=s, **dev)
+    s.synchronize()
+    check_sum("pipeline_sum", float(out.cpu()[0]), ref, inp, 1 << 20)
+
+
+def test_status_codes_on_device(suite_pkg):
+    import ctypes
+    e = suite_pkg["dot"]
+    x = torch.zeros(1024, device="cuda")
+    out = torch.empty(1, device="cuda")
+    ws = torch.empty(e.workspace_size(1024), dtype=torch.uint8, device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    assert e.call_raw(p(x), p(x), ctypes.c_int64(1024), p(out), p(ws), ctypes.c_size_t(8)) == 2
+    assert e.call_raw(p(x), p(x), ctypes.c_int64(1024), p(out), p(ws),
+                      ctypes.c_size_t(ws.numel())) == 0
+    m = suite_pkg["relu"]
+    assert m.call_raw(p(x), ctypes.c_int64(0), p(out), None, ctypes.c_size_t(0)) == 0
