@@ -1,0 +1,79 @@
+"""Command line with the shape of ``loomc compile|package --target cuda``
+(``src/loom_cli/main.ml:305-346``, flags at ``:443-458``):
+
+    python -m loom_b200 package --project DIR --out OUT [--kind shared|static]
+                                [--module M ...] [--entry E ...]
+                                [--enable-opt FLAG ...] [--no-multi-gpu]
+    python -m loom_b200 compile FILE --entry E --target cuda --out OUT
+                                [--enable-opt FLAG ...]
+
+Entries are read from ``*.tensor_ir.json`` files (the TensorIR the reference
+front end dumps with ``--emit tensor-ir``); ``--cuda-arch`` is accepted for
+compatibility and must name sm_100a.
+"""
+
+from __future__ import annotations
+
+import argparse
+import sys
+
+from . import artifact
+from .tensor_ir import TensorIRError
+
+
+def _options(ns) -> artifact.Options:
+    enabled = []
+    for item in ns.enable_opt or []:
+        enabled += [f for f in item.split(",") if f]
+    disabled = set()
+    for item in ns.disable_opt or []:
+        disabled |= {f for f in item.split(",") if f}
+    return artifact.Options(enabled=[f for f in enabled if f not in disabled],
+                            multi_gpu=not ns.no_multi_gpu,
+                            kind=getattr(ns, "kind", "shared"))
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(prog="python -m loom_b200")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+
+    def common(p):
+        p.add_argument("--out", required=True)
+        p.add_argument("--target", default="cuda", choices=["cuda"])
+        p.add_argument("--cuda-arch", default="sm_100a")
+        p.add_argument("--cuda-platform", default="current")
+        p.add_argument("--enable-opt", action="append")
+        p.add_argument("--disable-opt", action="append")
+        p.add_argument("--no-multi-gpu", action="store_true")
+
+    pk = sub.add_parser("package", help="package every entry of a project")
+    pk.add_argument("--project", required=True)
+    pk.add_argument("--kind", default="shared", choices=["shared", "static"])
+    pk.add_argument("--module", action="append", default=[])
+    pk.add_argument("--entry", action="append", default=[])
+    common(pk)
+
+    cp = sub.add_parser("compile", help="compile one entry")
+    cp.add_argument("file")
+    cp.add_argument("--entry", required=True)
+    cp.add_argument("--emit", default="all")
+    common(cp)
+
+    ns = ap.parse_args(argv)
+    if ns.cuda_arch not in ("sm_100a", "sm_100"):
+        print(f"error: this backend targets sm_100a only (got {ns.cuda_arch})", file=sys.stderr)
+        return 2
+    try:
+        if ns.cmd == "package":
+            res = artifact.generate_package(ns.project, ns.out, _options(ns), ns.module, ns.entry)
+        else:
+            res = artifact.compile_entry(ns.file, ns.entry, ns.out, _options(ns))
+    except (TensorIRError, artifact.BuildError) as exc:
+        print(f"error: {exc}", file=sys.stderr)
+        return 1
+    print(res.artifact_path)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
