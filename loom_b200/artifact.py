@@ -51,6 +51,8 @@ class Options:
     kind: str = "shared"          # "shared" | "static"
     nvcc: str = "nvcc"
     extra_nvcc_flags: List[str] = field(default_factory=list)
+    # reduction entries that also get a <sym>_noalloc variant (static scratch)
+    noalloc_entries: List[str] = field(default_factory=list)
 
     @property
     def async_return(self) -> bool:
@@ -188,6 +190,11 @@ def _entry_json(b: EntryBundle, files: List[str], package: str, multi_gpu: bool)
     return d
 
 
+def _noalloc_symbols(bundles, opts) -> List[str]:
+    return [b.plan.symbol + "_noalloc" for b in bundles
+            if b.program.entry_name in opts.noalloc_entries]
+
+
 def _manifest(mode, project_root, package, opts, artifact, header, source, entry_files,
               commands) -> str:
     obj = {
@@ -208,6 +215,8 @@ def _manifest(mode, project_root, package, opts, artifact, header, source, entry
         "optimizations": opts.to_json(),
         "build_commands": commands,
     }
+    if opts.noalloc_entries:
+        obj["noalloc_symbols"] = _noalloc_symbols([b for b, _ in entry_files], opts)
     if opts.multi_gpu:
         obj["comm_symbols"] = [line.split("(")[0].split()[-1]
                                for line in codegen.comm_prototypes(package)]
@@ -313,9 +322,10 @@ def generate_package(project_root: str, out_dir: str, opts: Optional[Options] = 
     ext = "so" if opts.kind == "shared" else "a"
     artifact = os.path.join(out_dir, f"lib{package}.{ext}")
     plans = [b.plan for b in bundles]
-    _write(header, codegen.render_header(package, plans, opts.multi_gpu))
+    _write(header, codegen.render_header(package, plans, opts.multi_gpu, opts.noalloc_entries))
     _write(source, codegen.render_source(package, f"loom/{package}.h", plans,
-                                         opts.async_return, opts.multi_gpu))
+                                         opts.async_return, opts.multi_gpu,
+                                         opts.noalloc_entries))
     entry_files = [(b, _write_entry_dir(out_dir, b)) for b in bundles]
     commands = build_artifact(opts, include_root, source, artifact) if build else \
         [shlex.join(nvcc_command(opts, include_root, source, artifact))]

@@ -21,6 +21,11 @@ BUILT_DIR = os.path.join(HERE, "_built")
 SUITE_DIR = os.path.join(BUILT_DIR, "b200_suite")
 
 
+def SUITE_OPTIONS() -> artifact.Options:
+    """Reference default flags, plus the static-scratch variant of dot."""
+    return artifact.Options(noalloc_entries=["dot"])
+
+
 def _newest_source_mtime() -> float:
     newest = 0.0
     for root in (SUITE_PROJECT, os.path.join(HERE, "csrc")):
@@ -39,7 +44,7 @@ def suite_is_current() -> bool:
 def build_suite(force: bool = False) -> artifact.PackageResult:
     if not force and suite_is_current():
         return None
-    return artifact.generate_package(SUITE_PROJECT, SUITE_DIR, artifact.Options())
+    return artifact.generate_package(SUITE_PROJECT, SUITE_DIR, SUITE_OPTIONS())
 
 
 def load_suite() -> Package:

@@ -36,7 +36,8 @@ def declared_symbols(path):
 
 def test_committed_header_is_the_generated_one(built):
     plans = [b.plan for b in discover_entries(B.SUITE_PROJECT)]
-    assert open(HEADER).read() == codegen.render_header("b200_suite", plans)
+    assert open(HEADER).read() == codegen.render_header("b200_suite", plans, True,
+                                                        B.SUITE_OPTIONS().noalloc_entries)
     assert open(os.path.join(built, "include", "loom", "b200_suite.h")).read() == \
         open(HEADER).read()
 
