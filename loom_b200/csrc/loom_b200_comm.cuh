@@ -151,10 +151,12 @@ inline int dist_local(const Ptrs<Body::kInputs>& in, int64_t n_local, const Body
   RankSlots<Op> slots(workspace, n_local);
   auto* partials = reinterpret_cast<typename Op::Acc*>(workspace_base(workspace));
   if (n_local == 0) {
-    reduce_finalize_kernel<Op><<<1, kThreads, 0, stream>>>(partials, 0, nullptr, slots.local);
+    reduce_finalize_kernel<Op><<<1, kFinalizeThreads, 0, stream>>>(partials, 0, nullptr,
+                                                                    slots.local);
     return launch_status();
   }
-  return launch_reduce<Op>(in, n_local, body, partials, nullptr, slots.local, stream);
+  return launch_reduce<Op>(in, n_local, body, partials, partial_capacity(n_local), nullptr,
+                           slots.local, stream);
 }
 
 // Phase 2: the scalar collective (sum: all-gather of fp64; max: all-reduce).

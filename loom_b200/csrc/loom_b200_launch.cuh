@@ -4,12 +4,12 @@
 // They replace the launch arithmetic of the reference's emitted wrapper
 // (src/loom_backend_cuda/cuda_backend.ml:1828-2270 and the support helpers at
 // :2344-2422): instead of fixed block-count caps (4096 / 32768 blocks of 256
-// threads) and a host loop of combine launches, the grid is sized from the
-// device's SM count times the resident CTAs per SM of the kernel actually
-// launched, and a reduction is always exactly two launches.
+// threads) and a host loop of combine launches, every kernel gets one CTA per
+// tile (a reduction at most kMaxPartials CTAs, or fewer when the caller's
+// scratch has fewer partial slots), and a reduction is always exactly two
+// launches.
 //
-// Nothing here allocates device memory and nothing holds device state: the
-// caches below hold only device attributes and occupancy numbers.
+// Nothing here allocates device memory and nothing holds device state.
 #pragma once
 
 #include <atomic>
@@ -36,10 +36,11 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 constexpr size_t kRankScratchBytes = 256;
 constexpr int kMaxRanks = 24;
 
-// Number of CTA partial slots a reduction over n elements may use.  The
-// workspace size and every reduction launch use this same bound.
+// Number of CTA partial slots a reduction over n elements may use: one per
+// smallest tile, at most kMaxPartials.  The workspace size and every
+// workspace-backed reduction launch use this same bound.
 inline int64_t partial_capacity(int64_t n) {
-  int64_t c = ceil_div(n, kTileElems);
+  int64_t c = ceil_div(n, kMinTileElems);
   if (c < 1) c = 1;
   if (c > kMaxPartials) c = kMaxPartials;
   return c;
@@ -69,35 +70,6 @@ inline int current_device() {
   return dev;
 }
 
-inline int sm_count(int dev) {
-  static std::atomic<int> cache[kMaxDevices];
-  if (dev < 0 || dev >= kMaxDevices) return 148;
-  int v = cache[dev].load(std::memory_order_relaxed);
-  if (v > 0) return v;
-  if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) {
-    cudaGetLastError();
-    v = 148;
-  }
-  cache[dev].store(v, std::memory_order_relaxed);
-  return v;
-}
-
-// Resident CTAs per SM of `kernel` at kThreads threads, cached per device in
-// the caller-provided slot array (one array per kernel instantiation).
-template <class Kernel>
-inline int resident_ctas(std::atomic<int>* cache, int dev, Kernel kernel) {
-  if (dev < 0 || dev >= kMaxDevices) return 4;
-  int v = cache[dev].load(std::memory_order_relaxed);
-  if (v > 0) return v;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, kThreads, 0) != cudaSuccess ||
-      v <= 0) {
-    cudaGetLastError();
-    v = 4;
-  }
-  cache[dev].store(v, std::memory_order_relaxed);
-  return v;
-}
-
 inline bool aligned4(const void* p) { return ((uintptr_t)p & 3u) == 0; }
 
 template <int K>
@@ -125,68 +97,55 @@ inline int launch_status() {
   return cudaGetLastError() == cudaSuccess ? LOOM_STATUS_OK : LOOM_STATUS_CUDA_ERROR;
 }
 
+inline unsigned clamp_grid(int64_t g, int64_t cap) {
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (unsigned)g;
+}
+
 // out[i] = body(in[0][i], ...) for i in [0, n).
 template <class Body>
 inline int launch_map(float* out, const Ptrs<Body::kInputs>& in, int64_t n, const Body& body,
                       cudaStream_t stream) {
-  static std::atomic<int> occ_vec[kMaxDevices];
-  static std::atomic<int> occ_scalar[kMaxDevices];
   if (n <= 0) return LOOM_STATUS_OK;
   if (!pointers_aligned4(in, out)) return LOOM_STATUS_INVALID_ARGUMENT;
-  const int dev = current_device();
-  const int sms = sm_count(dev);
   if (congruent16(in, out)) {
+    constexpr int U = MapUnroll<Body::kInputs>::value;
     const int64_t head = head_elems(out, n);
     const int64_t nvec = (n - head) >> 2;
-    const int64_t cap = (int64_t)sms * resident_ctas(occ_vec, dev, map_vec_kernel<Body>);
-    int64_t grid = ceil_div(nvec, kTileVecs);
-    if (grid > cap) grid = cap;
-    if (grid < 1) grid = 1;
-    map_vec_kernel<Body><<<(unsigned)grid, kThreads, 0, stream>>>(out, in, n, head, body);
+    const unsigned grid = clamp_grid(ceil_div(nvec, (int64_t)kThreads * U), kMaxGrid);
+    map_vec_kernel<Body, U><<<grid, kThreads, 0, stream>>>(out, in, n, head, body);
   } else {
-    const int64_t cap = (int64_t)sms * resident_ctas(occ_scalar, dev, map_scalar_kernel<Body>);
-    int64_t grid = ceil_div(n, (int64_t)kThreads * kUnroll * 4);
-    if (grid > cap) grid = cap;
-    if (grid < 1) grid = 1;
-    map_scalar_kernel<Body><<<(unsigned)grid, kThreads, 0, stream>>>(out, in, n, body);
+    const unsigned grid = clamp_grid(ceil_div(n, (int64_t)kThreads * kScalarUnroll), kMaxGrid);
+    map_scalar_kernel<Body><<<grid, kThreads, 0, stream>>>(out, in, n, body);
   }
   return launch_status();
 }
 
 // Reduces body(in[...][i]) over [0, n) with Op into out[0] (fp32) and/or
-// partial_out[0] (Op::Acc).  `partials` must hold partial_capacity(n) slots.
+// partial_out[0] (Op::Acc).  `partials` must hold `max_partials` slots
+// (at least 1); the first kernel uses at most that many CTAs.
 template <class Op, class Body>
 inline int launch_reduce(const Ptrs<Body::kInputs>& in, int64_t n, const Body& body,
-                         typename Op::Acc* partials, float* out,
+                         typename Op::Acc* partials, int64_t max_partials, float* out,
                          typename Op::Acc* partial_out, cudaStream_t stream) {
-  static std::atomic<int> occ_vec[kMaxDevices];
-  static std::atomic<int> occ_scalar[kMaxDevices];
-  if (n <= 0) return LOOM_STATUS_INVALID_ARGUMENT;
+  if (n <= 0 || max_partials < 1) return LOOM_STATUS_INVALID_ARGUMENT;
   if (!pointers_aligned4(in, nullptr)) return LOOM_STATUS_INVALID_ARGUMENT;
-  const int dev = current_device();
-  const int sms = sm_count(dev);
-  const int64_t capacity = partial_capacity(n);
-  int64_t grid;
+  unsigned grid;
   if (congruent16(in, in.p[0])) {
+    constexpr int U = ReduceUnroll<Body::kInputs>::value;
     const int64_t head = head_elems(in.p[0], n);
     const int64_t nvec = (n - head) >> 2;
-    const int64_t cap = (int64_t)sms * resident_ctas(occ_vec, dev, reduce_vec_kernel<Op, Body>);
-    grid = ceil_div(nvec, kTileVecs);
-    if (grid > cap) grid = cap;
-    if (grid > capacity) grid = capacity;
-    if (grid < 1) grid = 1;
-    reduce_vec_kernel<Op, Body><<<(unsigned)grid, kThreads, 0, stream>>>(partials, in, n, head, body);
+    grid = clamp_grid(ceil_div(nvec, (int64_t)kThreads * U), max_partials);
+    reduce_vec_kernel<Op, Body, U><<<grid, kThreads, 0, stream>>>(partials, in, n, head, body);
   } else {
-    const int64_t cap = (int64_t)sms * resident_ctas(occ_scalar, dev, reduce_scalar_kernel<Op, Body>);
-    grid = ceil_div(n, (int64_t)kThreads * kUnroll * 4);
-    if (grid > cap) grid = cap;
-    if (grid > capacity) grid = capacity;
-    if (grid < 1) grid = 1;
-    reduce_scalar_kernel<Op, Body><<<(unsigned)grid, kThreads, 0, stream>>>(partials, in, n, body);
+    grid = clamp_grid(ceil_div(n, (int64_t)kThreads * kScalarUnroll), max_partials);
+    reduce_scalar_kernel<Op, Body><<<grid, kThreads, 0, stream>>>(partials, in, n, body);
   }
   int st = launch_status();
   if (st != LOOM_STATUS_OK) return st;
-  reduce_finalize_kernel<Op><<<1, kThreads, 0, stream>>>(partials, (int)grid, out, partial_out);
+  reduce_finalize_kernel<Op><<<1, kFinalizeThreads, 0, stream>>>(partials, (int)grid, out,
+                                                                  partial_out);
   return launch_status();
 }
 

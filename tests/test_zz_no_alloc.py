@@ -3,8 +3,9 @@ the library device memory (no workspace argument; the per-CTA partials live
 in a static device array inside the library).
 
 Checked through the C ABI against the regular workspace entry
-loom_kernels_dot on two calls in a row -- the second call is smaller than the
-first, so it runs over the first call's leftovers in the shared array -- with
+loom_kernels_dot on two calls in a row -- the first is large enough that the
+entry caps its grid at the array's 4096 slots, the second is smaller and runs
+over the first call's leftovers in the shared array -- with
 the tolerance the other sum tests use:
 |noalloc - dot| <= 1e-6 * max(1, log2 n) * max(|dot|, sqrt(sum (x_i*y_i)^2)).
 
@@ -38,7 +39,7 @@ def _bind(pkg):
 def test_noalloc_dot_matches_workspace_entry_on_two_calls(suite_pkg):
     noalloc = _bind(suite_pkg)
     dot = suite_pkg["dot"]
-    for call, n in enumerate([(1 << 22) + 3, 1001]):
+    for call, n in enumerate([(1 << 24) + 3, 1001]):
         inp = workloads.entry_inputs("dot", n, seed_offset=900 + call)
         x = torch.from_numpy(inp["x"]).cuda()
         y = torch.from_numpy(inp["y"]).cuda()
