@@ -410,7 +410,9 @@ def run_e2e(pkg, data, outs, n, args, world, comm):
     return {"value": round(step_bytes * world / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "steps": steps,
             "ms_per_step": round(ms, 3),
-            "path": "loom_kernels_<entry> (synchronous reference ABI), pinned host buffers"}
+            "path": ("loom_kernels_<entry> (synchronous reference ABI)" if world == 1 else
+                     "loom_kernels_<entry>_dist (one scalar NCCL collective per reduction)")
+            + ", pinned host buffers"}
 
 
 def cpu_baseline(log2n: int, seconds: float, threads: int = 0):

@@ -71,6 +71,15 @@ class Entry:
             self.dist_ws_fn = getattr(lib, meta["dist_workspace_symbol"])
             self.dist_ws_fn.argtypes = [ctypes.c_int64]
             self.dist_ws_fn.restype = ctypes.c_size_t
+        self.multi_fn = None
+        if meta.get("multi_symbol"):
+            self.multi_fn = getattr(lib, meta["multi_symbol"])
+            mtypes = [ctypes.c_float if p["kind"] == "scalar-f32" else ctypes.c_void_p
+                      for p in self.params]
+            self.multi_fn.argtypes = [ctypes.c_int, ctypes.c_void_p] + mtypes + [
+                ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                ctypes.c_void_p]
+            self.multi_fn.restype = ctypes.c_int
         self._ws: Dict[tuple, object] = {}
 
     # -- helpers ------------------------------------------------------------
@@ -162,6 +171,44 @@ class Entry:
         if status != 0:
             raise LoomError(self.symbol + "_dist", status)
         return out
+
+
+    def multi(self, comms: Sequence["Comm"], shards: Sequence[Dict[str, object]], outs=None):
+        """One process, one shard per device: ``shards[d]`` holds the tensor
+        inputs on ``comms[d]``'s device (scalars are taken from ``shards[0]``).
+        Returns (per-device outputs, host scalar or None)."""
+        if self.multi_fn is None:
+            raise RuntimeError(f"{self.package.name} was built without multi-GPU entries")
+        torch = _torch()
+        nd = len(comms)
+        if nd != len(shards) or nd == 0:
+            raise ValueError("one shard per communicator")
+        ns = [self._n(sh) for sh in shards]
+        if outs is None:
+            outs = [self.new_output(ns[d], shards[d][self.tensor_params[0]].device)
+                    for d in range(nd)]
+        keep = []
+        args = [ctypes.c_int(nd), (ctypes.c_void_p * nd)(*[c.handle for c in comms])]
+        for p in self.params:
+            if p["kind"] == "scalar-f32":
+                args.append(ctypes.c_float(float(shards[0][p["name"]])))
+            else:
+                for sh, n in zip(shards, ns):
+                    self._args({q["name"]: sh[q["name"]] for q in self.params}, n)
+                arr = (ctypes.c_void_p * nd)(*[sh[p["name"]].data_ptr() for sh in shards])
+                keep.append(arr)
+                args.append(ctypes.cast(arr, ctypes.c_void_p))
+        shard_n = (ctypes.c_int64 * nd)(*ns)
+        out_arr = (ctypes.c_void_p * nd)(*[o.data_ptr() for o in outs])
+        wss = [self.workspace(ns[d], outs[d].device, dist=True) for d in range(nd)]
+        ws_arr = (ctypes.c_void_p * nd)(*[w.data_ptr() if w is not None else 0 for w in wss])
+        ws_sz = (ctypes.c_size_t * nd)(*[w.numel() if w is not None else 0 for w in wss])
+        host = ctypes.c_float(float("nan"))
+        status = self.multi_fn(*args, shard_n, out_arr, ws_arr, ws_sz,
+                               ctypes.byref(host) if self.result_kind == "scalar" else None)
+        if status != 0:
+            raise LoomError(self.symbol + "_multi", status)
+        return outs, (float(host.value) if self.result_kind == "scalar" else None)
 
 
 class Comm:

@@ -1,0 +1,128 @@
+"""Multi-GPU entries against the oracle on the full (unsharded) input.
+
+* `_multi`: one process drives every visible GPU (up to 8), one contiguous
+  shard per device (`loom_b200.shard.shard_bounds`), one grouped NCCL
+  collective for reductions.
+* `_dist`: one process per GPU (2 ranks), the NCCL communicator's id
+  rendezvoused over a gloo process group.
+
+Maps must reproduce the oracle bit for bit once the shards are concatenated;
+reductions must give the same bits on every device, max exactly and sums to
+the bar of test_gpu_parity.  Skipped with fewer than 2 GPUs.
+"""
+
+import math
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from loom_b200 import workloads
+from loom_b200.shard import shard_bounds
+
+from test_gpu_parity import MAPS, check_sum
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")]
+
+ENTRIES = ["saxpy", "relu", "affine_relu", "dot", "l2_norm_sq", "max_value", "pipeline_sum"]
+
+
+def _check(entry, results, ref, full, n):
+    if entry in MAPS:
+        got = np.concatenate(results)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), entry
+        return
+    bits = {np.float32(r).view(np.uint32).item() for r in results}
+    assert len(bits) == 1, (entry, results)       # every device holds the same value
+    got = float(results[0])
+    if entry == "max_value":
+        assert got == float(np.float32(ref))
+    else:
+        check_sum(entry, got, ref, full, n)
+
+
+@pytest.mark.parametrize("n", [(1 << 22) + 3, 37, 3])
+def test_multi_one_process(suite_pkg, oracle, n):
+    devs = list(range(min(torch.cuda.device_count(), 8)))
+    comms = suite_pkg.comm_init_all(devs)
+    try:
+        bounds = shard_bounds(n, len(devs))
+        for entry in ENTRIES:
+            full = workloads.entry_inputs(entry, n, seed_offset=len(devs))
+            shards = [{k: (torch.from_numpy(np.ascontiguousarray(v[s:e])).to(f"cuda:{d}")
+                           if isinstance(v, np.ndarray) else v) for k, v in full.items()}
+                      for d, (s, e) in zip(devs, bounds)]
+            outs, host = suite_pkg[entry].multi(comms, shards)
+            for d in devs:
+                torch.cuda.synchronize(d)
+            results = [o.cpu().numpy() if entry in MAPS else float(o.cpu()[0]) for o in outs]
+            _check(entry, results, oracle.run(entry, full), full, n)
+            if entry not in MAPS:
+                assert host == results[0]
+    finally:
+        for c in comms:
+            c.destroy()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _dist_rank(rank, world, port, n, queue):
+    import datetime
+
+    import torch.distributed as dist
+
+    from loom_b200.build import load_suite
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    comm = None
+    try:
+        pkg = load_suite()
+        comm = pkg.comm_from_process_group()
+        start, stop = shard_bounds(n, world)[rank]
+        for entry in ENTRIES:
+            full = workloads.entry_inputs(entry, n, seed_offset=world + 100)
+            mine = {k: (torch.from_numpy(np.ascontiguousarray(v[start:stop])).cuda()
+                        if isinstance(v, np.ndarray) else v) for k, v in full.items()}
+            out = pkg[entry].dist(comm, **mine)
+            torch.cuda.synchronize()
+            res = out.cpu().numpy() if entry in MAPS else float(out.cpu()[0])
+            gathered = [None] * world
+            dist.all_gather_object(gathered, res)
+            if rank == 0:
+                queue.put((entry, gathered))
+    finally:
+        if comm is not None:
+            comm.destroy()
+        dist.destroy_process_group()
+
+
+def test_dist_one_process_per_gpu(oracle):
+    world, n = 2, (1 << 21) + 5
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dist_rank, args=(r, world, port, n, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        got = dict(queue.get(timeout=300) for _ in ENTRIES)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert all(p.exitcode == 0 for p in procs)
+    for entry in ENTRIES:
+        full = workloads.entry_inputs(entry, n, seed_offset=world + 100)
+        _check(entry, got[entry], oracle.run(entry, full), full, n)
