@@ -173,6 +173,99 @@ class Entry:
         return out
 
 
+    def call_host(self, out=None, comm: Optional["Comm"] = None, chunk_elems: int = 1 << 23,
+                  **inputs):
+        """Run on HOST inputs (CPU torch tensors, ideally pinned, or numpy
+        arrays) and return a CPU tensor.  The current CUDA device runs it.
+
+        Maps stream in chunks through two device slots per tensor: chunk c+1
+        is copied in (and computed) on one stream while chunk c is copied
+        out on another, so the host->device and device->host PCIe directions
+        run at the same time.  Reductions copy each input to the device once
+        and call the entry (the `_dist` entry when `comm` is given, so every
+        rank gets the global result).  Host memory must not be touched until
+        the call returns; it synchronises before returning."""
+        torch = _torch()
+        host = {}
+        for p in self.params:
+            v = inputs[p["name"]]
+            if p["kind"] == "tensor1-f32":
+                if not isinstance(v, torch.Tensor):
+                    v = torch.from_numpy(v)
+                if v.is_cuda or v.dtype != torch.float32 or not v.is_contiguous():
+                    raise TypeError(f"{self.name}: {p['name']} must be a contiguous float32 "
+                                    "host tensor")
+            host[p["name"]] = v
+        n = int(host[self.tensor_params[0]].numel())
+        for t in self.tensor_params:
+            if host[t].numel() != n:
+                raise ValueError(f"{self.name}: tensor inputs must share one length")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        if out is None:
+            out = torch.empty(n if self.result_kind == "tensor" else 1, dtype=torch.float32,
+                              pin_memory=True)
+        st = self._host_state(dev, chunk_elems if self.result_kind == "tensor" else n)
+        s_in, s_out = st["streams"]
+        cur = torch.cuda.current_stream(dev)
+        s_in.wait_stream(cur)
+        if self.result_kind == "scalar":
+            with torch.cuda.stream(s_in):
+                dev_in = {t: st["slots"][t][0][:n] for t in self.tensor_params}
+                for t in self.tensor_params:
+                    dev_in[t].copy_(host[t], non_blocking=True)
+                args = {**{k: v for k, v in host.items() if k not in dev_in}, **dev_in}
+                res = st["out"][0]
+                if comm is not None:
+                    self.dist(comm, out=res, stream=s_in, **args)
+                else:
+                    self(out=res, stream=s_in, **args)
+                out.copy_(res, non_blocking=True)
+            s_in.synchronize()
+            return out
+        chunk = st["chunk"]
+        for c, off in enumerate(range(0, n, chunk)):
+            ln = min(chunk, n - off)
+            slot = c % 2
+            if c >= 2:
+                s_in.wait_event(st["drained"][slot])
+            with torch.cuda.stream(s_in):
+                dev_in = {t: st["slots"][t][slot][:ln] for t in self.tensor_params}
+                for t in self.tensor_params:
+                    dev_in[t].copy_(host[t][off:off + ln], non_blocking=True)
+                args = {**{k: v for k, v in host.items() if k not in dev_in}, **dev_in}
+                res = st["out"][slot][:ln]
+                self(out=res, stream=s_in, **args)
+                st["computed"][slot].record(s_in)
+            s_out.wait_event(st["computed"][slot])
+            with torch.cuda.stream(s_out):
+                out[off:off + ln].copy_(res, non_blocking=True)
+                st["drained"][slot].record(s_out)
+        s_out.synchronize()
+        s_in.synchronize()
+        return out
+
+    def _host_state(self, dev, chunk: int):
+        """Per-device streams, events and device slots of call_host (cached,
+        grown on demand)."""
+        torch = _torch()
+        key = str(dev)
+        st = self._ws.get(("host", key))
+        chunk = max(1, int(chunk))
+        if st is None or st["chunk"] < chunk:
+            nslots = 2 if self.result_kind == "tensor" else 1
+            st = {
+                "chunk": chunk,
+                "streams": (torch.cuda.Stream(dev), torch.cuda.Stream(dev)),
+                "slots": {t: [torch.empty(chunk, dtype=torch.float32, device=dev)
+                              for _ in range(nslots)] for t in self.tensor_params},
+                "out": [torch.empty(chunk if self.result_kind == "tensor" else 1,
+                                    dtype=torch.float32, device=dev) for _ in range(nslots)],
+                "computed": [torch.cuda.Event() for _ in range(2)],
+                "drained": [torch.cuda.Event() for _ in range(2)],
+            }
+            self._ws[("host", key)] = st
+        return st
+
     def multi(self, comms: Sequence["Comm"], shards: Sequence[Dict[str, object]], outs=None):
         """One process, one shard per device: ``shards[d]`` holds the tensor
         inputs on ``comms[d]``'s device (scalars are taken from ``shards[0]``).
