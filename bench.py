@@ -442,8 +442,8 @@ def cpu_baseline(log2n: int, seconds: float, threads: int = 0):
     from loom_b200 import workloads
     from oracle.loom_oracle import Oracle, load_programs
     threads = threads or len(os.sched_getaffinity(0))
-    oracle = Oracle(load_programs(os.path.join(ROOT, "loom_b200", "suite",
-                                               "kernels.tensor_ir.json")), name="b200_suite")
+    oracle = Oracle(load_programs(os.path.join(ROOT, "oracle",
+                                               "suite_kernels.tensor_ir.json")), name="b200_suite")
     n = 1 << log2n
     inputs = {e: workloads.entry_inputs(e, n) for e in ENTRIES}
     for e in ENTRIES:
@@ -474,8 +474,8 @@ def run_reference(args) -> None:
     from loom_b200 import workloads
     from oracle.loom_oracle import Oracle, load_programs
     threads = base["cores"]
-    oracle = Oracle(load_programs(os.path.join(ROOT, "loom_b200", "suite",
-                                               "kernels.tensor_ir.json")), name="b200_suite")
+    oracle = Oracle(load_programs(os.path.join(ROOT, "oracle",
+                                               "suite_kernels.tensor_ir.json")), name="b200_suite")
     n = 1 << args.cpu_log2
     inputs = {e: workloads.entry_inputs(e, n) for e in ENTRIES}
     for _ in range(args.warmup):

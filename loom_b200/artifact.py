@@ -89,17 +89,34 @@ def load_entries_file(path: str) -> List[Program]:
     return [program_from_json(item) for item in items]
 
 
+def _defines_entries(path: str) -> bool:
+    with open(path, "r", encoding="utf-8") as fh:
+        text = fh.read()
+    return "loom.entry" in text or "@entry" in text
+
+
+def load_source_file(path: str) -> List[Program]:
+    """Programs of one source: a ``*.tensor_ir.json`` (one program or a list)
+    or a Python module of ``@loom.entry`` functions (through the front end)."""
+    if path.endswith(".py"):
+        from .frontend import python_programs
+        return python_programs(path)
+    return load_entries_file(path)
+
+
 def discover_entries(project_root: str, module_filters: Sequence[str] = (),
                      entry_filters: Sequence[str] = ()) -> List[EntryBundle]:
     """Collect entries of a project (cuda_backend.ml:158-178, 307-326): every
-    ``*.tensor_ir.json`` below the root, skipping build and hidden dirs."""
-    skip = {"_build", "build", ".venv", ".git", ".hg", ".svn", "node_modules"}
+    ``*.tensor_ir.json`` and every Python module with ``@loom.entry``
+    functions below the root, skipping build and hidden dirs, in path order."""
+    skip = {"_build", "build", ".venv", ".git", ".hg", ".svn", "node_modules", "__pycache__"}
     found: List[str] = []
     for dirpath, dirnames, filenames in os.walk(project_root):
         dirnames[:] = sorted(d for d in dirnames if d not in skip and not d.startswith("."))
         for name in sorted(filenames):
-            if name.endswith(".tensor_ir.json"):
-                found.append(os.path.join(dirpath, name))
+            path = os.path.join(dirpath, name)
+            if name.endswith(".tensor_ir.json") or (name.endswith(".py") and _defines_entries(path)):
+                found.append(path)
     mfilt = [m.lower() for m in module_filters]
     efilt = [e.lower() for e in entry_filters]
     bundles: List[EntryBundle] = []
@@ -107,7 +124,7 @@ def discover_entries(project_root: str, module_filters: Sequence[str] = (),
         module = module_name_of_file(path)
         if mfilt and module.lower() not in mfilt:
             continue
-        for prog in load_entries_file(path):
+        for prog in load_source_file(path):
             if efilt and prog.entry_name.lower() not in efilt:
                 continue
             bundles.append(EntryBundle(module, path, prog, plan_entry(prog, module)))
@@ -344,7 +361,7 @@ def compile_entry(source_file: str, entry_name: str, out_dir: str,
     """``loomc compile <file> --entry e --target cuda`` (cuda_backend.ml:2675-2731)."""
     opts = opts or Options()
     module = module_name_of_file(source_file)
-    progs = [p for p in load_entries_file(source_file) if p.entry_name == entry_name]
+    progs = [p for p in load_source_file(source_file) if p.entry_name == entry_name]
     if not progs:
         raise TensorIRError(f"entry {entry_name!r} not found in {source_file}")
     prog = progs[0]

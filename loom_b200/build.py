@@ -28,11 +28,11 @@ def SUITE_OPTIONS() -> artifact.Options:
 
 def _newest_source_mtime() -> float:
     newest = 0.0
-    for root in (SUITE_PROJECT, os.path.join(HERE, "csrc")):
+    for root in (SUITE_PROJECT, os.path.join(HERE, "csrc"), HERE, os.path.join(HERE, "frontend")):
         for name in os.listdir(root):
-            newest = max(newest, os.path.getmtime(os.path.join(root, name)))
-    for name in ("codegen.py", "plan.py", "render.py", "artifact.py", "tensor_ir.py"):
-        newest = max(newest, os.path.getmtime(os.path.join(HERE, name)))
+            path = os.path.join(root, name)
+            if os.path.isfile(path):
+                newest = max(newest, os.path.getmtime(path))
     return newest
 
 
@@ -54,3 +54,19 @@ def load_suite() -> Package:
             f"{lib} is missing: build it with `python -c 'import loom_b200.build as b; "
             "b.build_suite()'` (needs nvcc)")
     return Package(SUITE_DIR)
+
+
+def build_project(project_dir: str, force: bool = False) -> str:
+    """Package any project into ``loom_b200/_built/<package>/`` (reference
+    default flags) and return that directory; skipped when the library is
+    newer than the project's sources and the backend."""
+    name = artifact.package_name_of_root(project_dir)
+    out = os.path.join(BUILT_DIR, name)
+    lib = os.path.join(out, f"lib{name}.so")
+    newest = _newest_source_mtime()
+    for root, _, files in os.walk(project_dir):
+        for f in files:
+            newest = max(newest, os.path.getmtime(os.path.join(root, f)))
+    if force or not os.path.exists(lib) or os.path.getmtime(lib) < newest:
+        artifact.generate_package(project_dir, out, artifact.Options())
+    return out

@@ -29,6 +29,29 @@ from typing import List, Sequence
 from .plan import EntryPlan, c_ident
 from .tensor_ir import ScalarParam, TensorParam
 
+# Names the generated C ABI uses for its own parameters, plus C/C++ keywords:
+# a user parameter with one of these names is renamed p_<name> in C.
+_RESERVED = {
+    "n", "out", "workspace", "workspace_size", "stream", "comm", "n_local", "ndev", "comms",
+    "shard_n", "host_result",
+    "alignas", "alignof", "and", "asm", "auto", "bool", "break", "case", "catch", "char",
+    "class", "const", "constexpr", "continue", "decltype", "default", "delete", "do", "double",
+    "else", "enum", "explicit", "export", "extern", "false", "float", "for", "friend", "goto",
+    "if", "inline", "int", "long", "mutable", "namespace", "new", "noexcept", "not", "nullptr",
+    "operator", "or", "private", "protected", "public", "register", "return", "short",
+    "signed", "sizeof", "static", "struct", "switch", "template", "this", "throw", "true",
+    "try", "typedef", "typeid", "typename", "union", "unsigned", "using", "virtual", "void",
+    "volatile", "while", "xor",
+}
+
+
+def cparam(name: str) -> str:
+    """C name of an entry parameter in the generated ABI."""
+    if name in _RESERVED or name.lower().startswith("loom"):
+        return "p_" + name
+    return name
+
+
 STATUS_DEFINES = [
     ("LOOM_STATUS_OK", 0),
     ("LOOM_STATUS_INVALID_ARGUMENT", 1),
@@ -42,9 +65,9 @@ def _param_decls(plan: EntryPlan) -> List[str]:
     out = []
     for p in plan.program.params:
         if isinstance(p, ScalarParam):
-            out.append(f"float {p.name}")
+            out.append(f"float {cparam(p.name)}")
         else:
-            out.append(f"const float* {p.name}")
+            out.append(f"const float* {cparam(p.name)}")
     return out
 
 
@@ -52,14 +75,14 @@ def _multi_param_decls(plan: EntryPlan) -> List[str]:
     out = []
     for p in plan.program.params:
         if isinstance(p, ScalarParam):
-            out.append(f"float {p.name}")
+            out.append(f"float {cparam(p.name)}")
         else:
-            out.append(f"const float* const* {p.name}")
+            out.append(f"const float* const* {cparam(p.name)}")
     return out
 
 
 def _arg_names(plan: EntryPlan) -> List[str]:
-    return [p.name for p in plan.program.params]
+    return [cparam(p.name) for p in plan.program.params]
 
 
 def header_prototypes(plan: EntryPlan, multi_gpu: bool = True) -> List[str]:
@@ -169,18 +192,18 @@ def _validation(plan: EntryPlan, n_name: str = "n") -> List[str]:
         lines.append(f"  if ({n_name} < 0) return LOOM_STATUS_INVALID_ARGUMENT;")
     for p in plan.program.params:
         if isinstance(p, TensorParam):
-            lines.append(f"  if ({p.name} == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;")
+            lines.append(f"  if ({cparam(p.name)} == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;")
     lines.append("  if (out == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;")
     return lines
 
 
 def _body_setup(plan: EntryPlan, ptr_expr=lambda name: name) -> List[str]:
     name = f"LoomBody_{plan.symbol}"
-    lines = [f"  {name} body;"]
+    lines = [f"  {name} loom_body;"]
     for s in plan.scalar_args:
-        lines.append(f"  body.{c_ident(s)} = {s};")
-    ptrs = ", ".join(ptr_expr(p) for p in plan.slots)
-    lines.append(f"  const loomb::Ptrs<{len(plan.slots)}> in = {{{{{ptrs}}}}};")
+        lines.append(f"  loom_body.{c_ident(s)} = {cparam(s)};")
+    ptrs = ", ".join(ptr_expr(cparam(p)) for p in plan.slots)
+    lines.append(f"  const loomb::Ptrs<{len(plan.slots)}> loom_in = {{{{{ptrs}}}}};")
     return lines
 
 
@@ -207,29 +230,29 @@ def render_entry(plan: EntryPlan, async_return: bool, multi_gpu: bool = True,
     # stream form: validation + launch, never synchronises
     L.append(f'extern "C" int {sym}_stream({", ".join(full + ["void* stream"])}) {{')
     L += _validation(plan)
-    L.append(f"  const size_t needed_workspace = {plan.workspace_symbol}(n);")
-    L.append("  if (needed_workspace > 0 && (workspace == nullptr || workspace_size < "
-             "needed_workspace)) return LOOM_STATUS_WORKSPACE_TOO_SMALL;")
+    L.append(f"  const size_t loom_needed = {plan.workspace_symbol}(n);")
+    L.append("  if (loom_needed > 0 && (workspace == nullptr || workspace_size < "
+             "loom_needed)) return LOOM_STATUS_WORKSPACE_TOO_SMALL;")
     if plan.kind == "map":
         L.append("  (void)workspace;")
         L.append("  (void)workspace_size;")
     L += _body_setup(plan)
-    L.append("  cudaStream_t s = static_cast<cudaStream_t>(stream);")
+    L.append("  cudaStream_t loom_stream = static_cast<cudaStream_t>(stream);")
     if plan.kind == "map":
-        L.append("  return loomb::launch_map(out, in, n, body, s);")
+        L.append("  return loomb::launch_map(out, loom_in, n, loom_body, loom_stream);")
     else:
         acc = "double" if plan.reduce_kind == "sum" else "float"
-        L.append(f"  {acc}* partials = reinterpret_cast<{acc}*>(loomb::workspace_base(workspace));")
-        L.append(f"  return loomb::launch_reduce<{_op(plan)}>(in, n, body, partials, "
-                 "loomb::partial_capacity(n), out, nullptr, s);")
+        L.append(f"  {acc}* loom_partials = reinterpret_cast<{acc}*>(loomb::workspace_base(workspace));")
+        L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, loom_partials, "
+                 "loomb::partial_capacity(n), out, nullptr, loom_stream);")
     L.append("}")
     L.append("")
     # the reference entry: legacy default stream, synchronous unless built with
     # cuda-async-wrapper-return (cuda_backend.ml:2259-2267)
     L.append(f'extern "C" int {sym}({", ".join(full)}) {{')
     call_args = ", ".join(args + ["n", "out", "workspace", "workspace_size", "nullptr"])
-    L.append(f"  const int status = {sym}_stream({call_args});")
-    L.append("  if (status != LOOM_STATUS_OK) return status;")
+    L.append(f"  const int loom_status = {sym}_stream({call_args});")
+    L.append("  if (loom_status != LOOM_STATUS_OK) return loom_status;")
     L.append("  return LOOM_STATUS_OK;" if async_return else "  return loomb::finish_sync();")
     L.append("}")
     L.append("")
@@ -269,15 +292,15 @@ def _render_dist(plan: EntryPlan, async_return: bool) -> List[str]:
         L.append("  if (n_local < 0) return LOOM_STATUS_INVALID_ARGUMENT;")
         for p in plan.program.params:
             if isinstance(p, TensorParam):
-                L.append(f"  if (n_local > 0 && {p.name} == nullptr) return "
+                L.append(f"  if (n_local > 0 && {cparam(p.name)} == nullptr) return "
                          "LOOM_STATUS_INVALID_ARGUMENT;")
         L.append("  if (out == nullptr || comm == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;")
-        L.append(f"  const size_t needed_workspace = {sym}_dist_workspace_size(n_local);")
-        L.append("  if (workspace == nullptr || workspace_size < needed_workspace) "
+        L.append(f"  const size_t loom_needed = {sym}_dist_workspace_size(n_local);")
+        L.append("  if (workspace == nullptr || workspace_size < loom_needed) "
                  "return LOOM_STATUS_WORKSPACE_TOO_SMALL;")
         L += _body_setup(plan)
         op = _op(plan)
-        L.append(f"  return loomb::dist_reduce<{op}>(in, n_local, body, workspace, out, "
+        L.append(f"  return loomb::dist_reduce<{op}>(loom_in, n_local, loom_body, workspace, out, "
                  "static_cast<loomb::Comm*>(comm), static_cast<cudaStream_t>(stream));")
     L += ["}", ""]
     return L
@@ -296,69 +319,69 @@ def _render_multi(plan: EntryPlan, async_return: bool) -> List[str]:
              " || out == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;")
     for p in plan.program.params:
         if isinstance(p, TensorParam):
-            L.append(f"  if ({p.name} == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;")
-    L.append("  for (int d = 0; d < ndev; ++d) {")
-    out_null = "out[d] == nullptr" if plan.kind == "reduce" else \
-        "(shard_n[d] > 0 && out[d] == nullptr)"
-    L.append(f"    if (comms[d] == nullptr || {out_null} || shard_n[d] < 0) "
+            L.append(f"  if ({cparam(p.name)} == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;")
+    L.append("  for (int loom_d = 0; loom_d < ndev; ++loom_d) {")
+    out_null = "out[loom_d] == nullptr" if plan.kind == "reduce" else \
+        "(shard_n[loom_d] > 0 && out[loom_d] == nullptr)"
+    L.append(f"    if (comms[loom_d] == nullptr || {out_null} || shard_n[loom_d] < 0) "
              "return LOOM_STATUS_INVALID_ARGUMENT;")
     for p in plan.program.params:
         if isinstance(p, TensorParam):
-            L.append(f"    if (shard_n[d] > 0 && {p.name}[d] == nullptr) "
+            L.append(f"    if (shard_n[loom_d] > 0 && {cparam(p.name)}[loom_d] == nullptr) "
                      "return LOOM_STATUS_INVALID_ARGUMENT;")
     if plan.uses_workspace:
-        L.append("    if (workspace == nullptr || workspace_size == nullptr || workspace[d] == nullptr"
-                 f" || workspace_size[d] < {sym}_dist_workspace_size(shard_n[d])) "
+        L.append("    if (workspace == nullptr || workspace_size == nullptr || workspace[loom_d] == nullptr"
+                 f" || workspace_size[loom_d] < {sym}_dist_workspace_size(shard_n[loom_d])) "
                  "return LOOM_STATUS_WORKSPACE_TOO_SMALL;")
     L.append("  }")
-    L.append("  loomb::DeviceGuard guard;")
-    L.append("  for (int d = 0; d < ndev; ++d) {")
-    L.append("    loomb::Comm* c = static_cast<loomb::Comm*>(comms[d]);")
-    L.append("    if (cudaSetDevice(c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
-    args = [f"{p.name}[d]" if isinstance(p, TensorParam) else p.name
+    L.append("  loomb::DeviceGuard loom_guard;")
+    L.append("  for (int loom_d = 0; loom_d < ndev; ++loom_d) {")
+    L.append("    loomb::Comm* loom_c = static_cast<loomb::Comm*>(comms[loom_d]);")
+    L.append("    if (cudaSetDevice(loom_c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
+    args = [f"{cparam(p.name)}[loom_d]" if isinstance(p, TensorParam) else cparam(p.name)
             for p in plan.program.params]
     if plan.kind == "map":
-        L.append("    if (shard_n[d] == 0) continue;")
-        L.append(f"    const int status = {sym}_stream({', '.join(args)}, shard_n[d], out[d], "
+        L.append("    if (shard_n[loom_d] == 0) continue;")
+        L.append(f"    const int loom_status = {sym}_stream({', '.join(args)}, shard_n[loom_d], out[loom_d], "
                  "nullptr, 0, nullptr);")
-        L.append("    if (status != LOOM_STATUS_OK) return status;")
+        L.append("    if (loom_status != LOOM_STATUS_OK) return loom_status;")
         L.append("  }")
         L.append("  (void)workspace;")
         L.append("  (void)workspace_size;")
         L.append("  (void)host_result;")
     else:
         op = _op(plan)
-        L += ["  " + line for line in _body_setup(plan, lambda name: f"{name}[d]")]
-        L.append(f"    const int status = loomb::dist_local<{op}>(in, shard_n[d], body, "
-                 "workspace[d], nullptr);")
-        L.append("    if (status != LOOM_STATUS_OK) return status;")
+        L += ["  " + line for line in _body_setup(plan, lambda name: f"{name}[loom_d]")]
+        L.append(f"    const int loom_status = loomb::dist_local<{op}>(loom_in, shard_n[loom_d], loom_body, "
+                 "workspace[loom_d], nullptr);")
+        L.append("    if (loom_status != LOOM_STATUS_OK) return loom_status;")
         L.append("  }")
         L.append("  if (loomb::nccl_group_start() != 0) return LOOM_STATUS_COMM_ERROR;")
-        L.append("  int group_status = LOOM_STATUS_OK;")
-        L.append("  for (int d = 0; d < ndev && group_status == LOOM_STATUS_OK; ++d) {")
-        L.append("    loomb::Comm* c = static_cast<loomb::Comm*>(comms[d]);")
-        L.append(f"    group_status = loomb::dist_collective<{op}>(workspace[d], shard_n[d], out[d], "
-                 "c, nullptr);")
+        L.append("  int loom_group_status = LOOM_STATUS_OK;")
+        L.append("  for (int loom_d = 0; loom_d < ndev && loom_group_status == LOOM_STATUS_OK; ++loom_d) {")
+        L.append("    loomb::Comm* loom_c = static_cast<loomb::Comm*>(comms[loom_d]);")
+        L.append(f"    loom_group_status = loomb::dist_collective<{op}>(workspace[loom_d], shard_n[loom_d], out[loom_d], "
+                 "loom_c, nullptr);")
         L.append("  }")
         L.append("  if (loomb::nccl_group_end() != 0) return LOOM_STATUS_COMM_ERROR;")
-        L.append("  if (group_status != LOOM_STATUS_OK) return group_status;")
-        L.append("  for (int d = 0; d < ndev; ++d) {")
-        L.append("    loomb::Comm* c = static_cast<loomb::Comm*>(comms[d]);")
-        L.append("    if (cudaSetDevice(c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
-        L.append(f"    const int status = loomb::dist_finish<{op}>(workspace[d], shard_n[d], out[d], "
-                 "c, nullptr);")
-        L.append("    if (status != LOOM_STATUS_OK) return status;")
+        L.append("  if (loom_group_status != LOOM_STATUS_OK) return loom_group_status;")
+        L.append("  for (int loom_d = 0; loom_d < ndev; ++loom_d) {")
+        L.append("    loomb::Comm* loom_c = static_cast<loomb::Comm*>(comms[loom_d]);")
+        L.append("    if (cudaSetDevice(loom_c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
+        L.append(f"    const int loom_status = loomb::dist_finish<{op}>(workspace[loom_d], shard_n[loom_d], out[loom_d], "
+                 "loom_c, nullptr);")
+        L.append("    if (loom_status != LOOM_STATUS_OK) return loom_status;")
         L.append("  }")
         L.append("  if (host_result != nullptr) {")
-        L.append("    loomb::Comm* c0 = static_cast<loomb::Comm*>(comms[0]);")
-        L.append("    if (cudaSetDevice(c0->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
+        L.append("    loomb::Comm* loom_c0 = static_cast<loomb::Comm*>(comms[0]);")
+        L.append("    if (cudaSetDevice(loom_c0->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
         L.append("    if (cudaMemcpy(host_result, out[0], sizeof(float), cudaMemcpyDeviceToHost) != "
                  "cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
         L.append("  }")
     if not async_return:
-        L.append("  for (int d = 0; d < ndev; ++d) {")
-        L.append("    loomb::Comm* c = static_cast<loomb::Comm*>(comms[d]);")
-        L.append("    if (cudaSetDevice(c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
+        L.append("  for (int loom_d = 0; loom_d < ndev; ++loom_d) {")
+        L.append("    loomb::Comm* loom_c = static_cast<loomb::Comm*>(comms[loom_d]);")
+        L.append("    if (cudaSetDevice(loom_c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
         L.append("    if (loomb::finish_sync() != LOOM_STATUS_OK) return LOOM_STATUS_CUDA_ERROR;")
         L.append("  }")
     L.append("  return LOOM_STATUS_OK;")
@@ -451,13 +474,13 @@ def render_noalloc(plan: EntryPlan) -> str:
         f'extern "C" int {sym}_noalloc({", ".join(decls)}) {{',
     ]
     L += _validation(plan)
-    L.append(f"  const int64_t slots = (int64_t)(sizeof(loom_noalloc_scratch) / sizeof({acc}));")
-    L.append("  void* scratch = nullptr;")
-    L.append("  const int status = loom_noalloc_scratch_on(loomb::current_device(), &scratch);")
-    L.append("  if (status != LOOM_STATUS_OK) return status;")
+    L.append(f"  const int64_t loom_slots = (int64_t)(sizeof(loom_noalloc_scratch) / sizeof({acc}));")
+    L.append("  void* loom_scratch = nullptr;")
+    L.append("  const int loom_status = loom_noalloc_scratch_on(loomb::current_device(), &loom_scratch);")
+    L.append("  if (loom_status != LOOM_STATUS_OK) return loom_status;")
     L += _body_setup(plan)
-    L.append(f"  return loomb::launch_reduce<{_op(plan)}>(in, n, body, static_cast<{acc}*>(scratch), "
-             "slots, out, nullptr, static_cast<cudaStream_t>(stream));")
+    L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, static_cast<{acc}*>(loom_scratch), "
+             "loom_slots, out, nullptr, static_cast<cudaStream_t>(stream));")
     L += ["}", ""]
     return "\n".join(L)
 

@@ -7,7 +7,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
-SUITE_IR = os.path.join(ROOT, "loom_b200", "suite", "kernels.tensor_ir.json")
+SUITE_IR = os.path.join(ROOT, "oracle", "suite_kernels.tensor_ir.json")
 
 
 def pytest_configure(config):

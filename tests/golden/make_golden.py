@@ -10,8 +10,10 @@ nothing at test time reads it):
   copied verbatim;
 * ``front_ir/<module>.<entry>.json``: FrontIR that the reference's Python
   frontend (``src/frontends/python/loom_frontend_python.py front-ir-json``)
-  prints for the suite entries and for the reference's Python examples and
-  package fixture.
+  prints for the suite entries, for ``sources/cases/frontend_cases.py`` and for the
+  reference's Python examples and package fixture;
+* ``front_ir_errors.json``: the reference frontend's error message for each
+  entry of ``sources/errors/frontend_errors.py``.
 """
 
 import json
@@ -33,6 +35,9 @@ def main(ref: str) -> None:
     sources = {
         os.path.join(ROOT, "loom_b200", "suite", "kernels.py"):
             ["saxpy", "relu", "dot", "l2_norm_sq", "max_value", "affine_relu", "pipeline_sum"],
+        os.path.join(HERE, "sources", "cases", "frontend_cases.py"):
+            ["nested_helpers", "clamp_scale", "tuple_lets", "soft_threshold", "hypot_sum",
+             "neg_max", "ratio_exp", "select_floor", "scaled_chain"],
         os.path.join(ref, "examples", "saxpy.py"): ["saxpy"],
         os.path.join(ref, "examples", "relu.py"): ["relu"],
         os.path.join(ref, "examples", "dot.py"): ["dot"],
@@ -53,6 +58,18 @@ def main(ref: str) -> None:
             with open(os.path.join(out_front, f"{tag}.{entry}.json"), "w") as fh:
                 json.dump(obj, fh, indent=1, sort_keys=True)
                 fh.write("\n")
+    errors = {}
+    bad = os.path.join(HERE, "sources", "errors", "frontend_errors.py")
+    for entry in ("with_loop", "tensor_capture", "chained", "keyword_call", "wrong_return",
+                  "unknown_call", "tensor_branch"):
+        proc = subprocess.run([sys.executable, frontend, "front-ir-json", bad, "--entry", entry],
+                              capture_output=True, text=True)
+        errors[entry] = {"returncode": proc.returncode,
+                         "stderr": proc.stderr.strip().splitlines()[-1] if proc.stderr.strip()
+                         else ""}
+    with open(os.path.join(HERE, "front_ir_errors.json"), "w") as fh:
+        json.dump(errors, fh, indent=1, sort_keys=True)
+        fh.write("\n")
     print("golden fixtures written to", HERE)
 
 

@@ -15,7 +15,7 @@ from loom_b200 import workloads
 from loom_b200.shard import shard_bounds
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-SUITE_IR = os.path.join(ROOT, "loom_b200", "suite", "kernels.tensor_ir.json")
+SUITE_IR = os.path.join(ROOT, "oracle", "suite_kernels.tensor_ir.json")
 N = 100_003
 
 
