@@ -77,6 +77,9 @@ def read_traffic():
 
 
 class ClockSampler:
+    """nvidia-smi samples of one GPU every 100 ms, time-stamped on arrival by
+    a reader thread; only the samples inside [mark_start, mark_end] count."""
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -84,8 +87,16 @@ class ClockSampler:
     def __init__(self, gpu_id: str):
         self.gpu_id = gpu_id
         self.proc = None
+        self.lines = []
+        self.t0 = self.t1 = None
+        self.thread = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line))
 
     def start(self):
+        import threading
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -93,20 +104,42 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def wait_first(self, timeout: float = 10.0):
+        end = time.time() + timeout
+        while self.proc is not None and not self.lines and time.time() < end:
+            time.sleep(0.05)
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
 
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=10)
+            self.proc.wait(timeout=10)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            out, _ = self.proc.communicate()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        t0 = self.t0 if self.t0 is not None else 0.0
+        t1 = self.t1 if self.t1 is not None else float("inf")
+        rows = [line for t, line in self.lines if t0 <= t <= t1 + 0.1]
+        if not rows and self.lines:       # region shorter than one period: nearest sample
+            mid = (t0 + t1) / 2 if self.t1 is not None else t0
+            rows = [min(self.lines, key=lambda tl: abs(tl[0] - mid))[1]]
         sm, mx, power, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
-            parts = [p.strip() for p in line.split(",")]
+        for line in rows:
+            parts = [q.strip() for q in line.split(",")]
             if len(parts) < 9:
                 continue
             try:
@@ -245,27 +278,29 @@ def run_ours(args) -> None:
             if events is not None:
                 events[i][1].record(stream)
 
+    props = torch.cuda.get_device_properties(local)
+    sampler = ClockSampler(f"GPU-{props.uuid}" if hasattr(props, "uuid") else str(local))
+    sampler.start()
+    sampler.wait_first()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
 
-    props = torch.cuda.get_device_properties(local)
-    sampler = ClockSampler(f"GPU-{props.uuid}" if hasattr(props, "uuid") else str(local))
-    sampler.start()
-    time.sleep(0.3)
     per_kernel = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                    for _ in calls] for _ in range(args.steps)]
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
+    sampler.mark_start()
     start.record(stream)
     for s in range(args.steps):
         step(per_kernel[s])
     end.record(stream)
     torch.cuda.synchronize()
+    sampler.mark_end()
     barrier(world)
     clocks = sampler.stop()
     elapsed_ms = start.elapsed_time(end)
@@ -514,6 +549,61 @@ def run_reference(args) -> None:
     }), flush=True)
 
 
+def run_pipeline_sweep(args) -> None:
+    """The fused-pipeline configuration swept over N (1 GPU): device time per
+    call of affine_relu (z = relu(a*x + y)) and pipeline_sum (sum(z*w)),
+    median of CUDA-event-timed calls; for N*12 bytes below 512 MiB a 512 MiB
+    buffer is rewritten before every timed call so that no input is served
+    from L2.  Prints one JSON line."""
+    import torch
+    from loom_b200.build import load_suite
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    pkg = load_suite()
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(128 << 20, dtype=torch.float32, device="cuda")
+    points = []
+    gen = torch.Generator(device="cuda")
+    for log2n in args.sweep:
+        n = 1 << log2n
+        gen.manual_seed(20260417 + log2n)
+        x = torch.rand(n, device="cuda", generator=gen).mul_(2).sub_(1)
+        y = torch.rand(n, device="cuda", generator=gen).mul_(2).sub_(1)
+        w = torch.rand(n, device="cuda", generator=gen).mul_(2).sub_(1)
+        z = torch.empty(n, device="cuda")
+        s = torch.empty(1, device="cuda")
+        reps = 200 if n <= (1 << 22) else (20 if n <= (1 << 28) else 5)
+        needs_flush = 12 * n < (512 << 20)
+        row = {"n": n, "log2n": log2n, "l2_flush": needs_flush}
+        for entry, call, nbytes in (
+                ("affine_relu", lambda: pkg["affine_relu"](out=z, stream=stream, x=x, y=y, a=0.75),
+                 12 * n),
+                ("pipeline_sum", lambda: pkg["pipeline_sum"](out=s, stream=stream, x=x, y=y, w=w,
+                                                             a=0.75), 12 * n)):
+            for _ in range(3):
+                call()
+            times = []
+            for _ in range(reps):
+                if needs_flush:
+                    flush.fill_(1.0)
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                call()
+                b.record(stream)
+                b.synchronize()
+                times.append(a.elapsed_time(b) * 1e3)
+            us = statistics.median(times)
+            row[entry + "_us"] = round(us, 2)
+            row[entry + "_gbs"] = round(nbytes / (us * 1e-6) / 1e9, 1)
+        points.append(row)
+        del x, y, w, z
+        torch.cuda.empty_cache()
+    print(json.dumps({"mode": "pipeline_sweep", "metric": METRIC, "unit": "GB/s",
+                      "config": {"workload": "fused pipeline: affine_relu z = relu(0.75*x + y) "
+                                             "and pipeline_sum s = sum(z*w), x, y, w ~ U(-1,1)"},
+                      "points": points}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -526,10 +616,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-log2", type=int, default=24)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--pipeline-sweep", action="store_true",
+                    help="time the fused pipeline over --sweep sizes instead of the suite step")
+    ap.add_argument("--sweep", type=int, nargs="*", default=[10, 14, 18, 22, 26, 30, 32])
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.pipeline_sweep:
+        run_pipeline_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -245,10 +245,39 @@ __device__ __forceinline__ float fold_chunks(const float (&c)[U]) {
   }
 }
 
+// Lets the finalize kernel, launched as a programmatic dependent of this
+// grid, be scheduled early; it still waits (griddepcontrol.wait) for this
+// whole grid to complete and its writes to be visible before reading.
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void wait_for_prerequisite_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// A one-CTA reduction is already complete in that CTA: it writes the result
+// itself and the launcher skips the finalize kernel.
+template <class Op>
+__device__ __forceinline__ void store_reduction(typename Op::Acc acc,
+                                                typename Op::Acc* __restrict__ partials,
+                                                float* __restrict__ out,
+                                                typename Op::Acc* __restrict__ partial_out) {
+  if (threadIdx.x != 0) return;
+  if (gridDim.x == 1) {
+    if (out != nullptr) out[0] = Op::to_float(acc);
+    if (partial_out != nullptr) partial_out[0] = acc;
+  } else {
+    partials[blockIdx.x] = acc;
+  }
+}
+
 template <class Op, class Body, int U>
 __global__ void __launch_bounds__(kThreads)
 reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInputs> in,
-                  const int64_t n, const int64_t head, const Body body) {
+                  const int64_t n, const int64_t head, const Body body, float* __restrict__ out,
+                  typename Op::Acc* __restrict__ partial_out) {
+  allow_dependent_launch();
   constexpr int K = Body::kInputs;
   constexpr int64_t kTile = (int64_t)kThreads * U;
   using Acc = typename Op::Acc;
@@ -292,13 +321,15 @@ reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInp
     if (i >= 0) acc = Op::absorb(acc, apply1(body, in, i));
   }
   acc = block_reduce<Op>(acc);
-  if (threadIdx.x == 0) partials[blockIdx.x] = acc;
+  store_reduction<Op>(acc, partials, out, partial_out);
 }
 
 template <class Op, class Body>
 __global__ void __launch_bounds__(kThreads)
 reduce_scalar_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInputs> in,
-                     const int64_t n, const Body body) {
+                     const int64_t n, const Body body, float* __restrict__ out,
+                     typename Op::Acc* __restrict__ partial_out) {
+  allow_dependent_launch();
   using Acc = typename Op::Acc;
   constexpr int kU = kScalarUnroll;
   constexpr int64_t kTile = (int64_t)kThreads * kU;
@@ -332,7 +363,7 @@ reduce_scalar_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::k
     }
   }
   acc = block_reduce<Op>(acc);
-  if (threadIdx.x == 0) partials[blockIdx.x] = acc;
+  store_reduction<Op>(acc, partials, out, partial_out);
 }
 
 // One CTA folds `count` CTA partials in a fixed order (four interleaved
@@ -345,6 +376,7 @@ reduce_finalize_kernel(const typename Op::Acc* __restrict__ partials, const int 
                        float* __restrict__ out, typename Op::Acc* __restrict__ partial_out) {
   using Acc = typename Op::Acc;
   constexpr int T = kFinalizeThreads;
+  wait_for_prerequisite_grid();  // no-op unless launched as a programmatic dependent
   Acc a0 = Op::init(), a1 = Op::init(), a2 = Op::init(), a3 = Op::init();
   int i = threadIdx.x;
   for (; i + 3 * T < count; i += 4 * T) {

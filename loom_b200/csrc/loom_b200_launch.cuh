@@ -97,6 +97,32 @@ inline int launch_status() {
   return cudaGetLastError() == cudaSuccess ? LOOM_STATUS_OK : LOOM_STATUS_CUDA_ERROR;
 }
 
+// The finalize CTA as a programmatic dependent launch of the kernel before
+// it on the stream: the hardware may schedule it while that kernel still
+// runs, and its griddepcontrol.wait holds it until that grid has completed.
+// Where the attribute is refused, a plain launch gives the same result.
+template <class Op>
+inline int launch_finalize(const typename Op::Acc* partials, int count, float* out,
+                           typename Op::Acc* partial_out, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kFinalizeThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, reduce_finalize_kernel<Op>, partials, count, out, partial_out) ==
+      cudaSuccess)
+    return LOOM_STATUS_OK;
+  cudaGetLastError();
+  reduce_finalize_kernel<Op><<<1, kFinalizeThreads, 0, stream>>>(partials, count, out,
+                                                                  partial_out);
+  return launch_status();
+}
+
 inline unsigned clamp_grid(int64_t g, int64_t cap) {
   if (g > cap) g = cap;
   if (g < 1) g = 1;
@@ -137,16 +163,16 @@ inline int launch_reduce(const Ptrs<Body::kInputs>& in, int64_t n, const Body& b
     const int64_t head = head_elems(in.p[0], n);
     const int64_t nvec = (n - head) >> 2;
     grid = clamp_grid(ceil_div(nvec, (int64_t)kThreads * U), max_partials);
-    reduce_vec_kernel<Op, Body, U><<<grid, kThreads, 0, stream>>>(partials, in, n, head, body);
+    reduce_vec_kernel<Op, Body, U><<<grid, kThreads, 0, stream>>>(partials, in, n, head, body,
+                                                                   out, partial_out);
   } else {
     grid = clamp_grid(ceil_div(n, (int64_t)kThreads * kScalarUnroll), max_partials);
-    reduce_scalar_kernel<Op, Body><<<grid, kThreads, 0, stream>>>(partials, in, n, body);
+    reduce_scalar_kernel<Op, Body><<<grid, kThreads, 0, stream>>>(partials, in, n, body, out,
+                                                                  partial_out);
   }
   int st = launch_status();
-  if (st != LOOM_STATUS_OK) return st;
-  reduce_finalize_kernel<Op><<<1, kFinalizeThreads, 0, stream>>>(partials, (int)grid, out,
-                                                                  partial_out);
-  return launch_status();
+  if (st != LOOM_STATUS_OK || grid == 1) return st;  // one CTA wrote the result itself
+  return launch_finalize<Op>(partials, (int)grid, out, partial_out, stream);
 }
 
 // Blocks until the device is idle, mapping the result to a status code (the
