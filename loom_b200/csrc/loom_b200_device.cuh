@@ -22,12 +22,13 @@
 //    and finishes a tail of 0..3 elements; otherwise it streams 32-bit
 //    elements;
 //  * one tile per CTA: a tile is kThreads x U float4 per input (U by the
-//    number of inputs, so every thread keeps 2-4 independent 16-byte loads in
-//    flight), and the grid has one CTA per tile, so the hardware scheduler
-//    hands tiles to SMs as they free up.  Measured on B200 this beats a
-//    persistent grid-stride loop (SM count x resident CTAs) by 13-16% for
-//    maps and 3-4% for reductions: the static stride leaves the slowest SMs
-//    with the tail;
+//    number of inputs, so every thread keeps 1-4 independent 16-byte loads per
+//    input in flight), and the grid has one CTA per tile, so the hardware
+//    scheduler hands tiles to SMs as they free up.  Measured on B200 this
+//    beats a persistent grid-stride loop (SM count x resident CTAs) by 13-16%
+//    for maps and 3-4% for reductions: the static stride leaves the slowest
+//    SMs with the tail.  Map kernels have no loop at all; reductions walk
+//    whole tiles with a grid stride only past kMaxPartials CTAs;
 //  * reductions: sums accumulate each thread's tile chunk in fp32 and fold
 //    the chunk into an fp64 per-thread accumulator; CTAs reduce with
 //    xor-shuffle butterflies and write one fp64 partial each to the caller's
@@ -106,45 +107,46 @@ __device__ __forceinline__ float apply1(const Body& body, const Ptrs<Body::kInpu
 // ---------------------------------------------------------------------------
 // element-wise map: out[i] = body(in_0[i], ..., in_{K-1}[i])
 
-// Vector path.  Preconditions (checked by the host launcher): every pointer
-// is 4-byte aligned and congruent to `out` mod 16; head = number of leading
-// elements before the first 16-byte boundary (0..3, at most n).
+// Vector path, one tile of kThreads x U float4 per CTA and no loop (the grid
+// covers every tile, which keeps the kernel at about 20 registers and the SMs
+// at full occupancy).  Preconditions (checked by the host launcher): every
+// pointer is 4-byte aligned and congruent to `out` mod 16; head = number of
+// leading elements before the first 16-byte boundary (0..3, at most n); the
+// grid is max(1, number of tiles).
 template <class Body, int U>
 __global__ void __launch_bounds__(kThreads)
 map_vec_kernel(float* __restrict__ out, const Ptrs<Body::kInputs> in, const int64_t n,
                const int64_t head, const Body body) {
   constexpr int K = Body::kInputs;
-  constexpr int64_t kTile = (int64_t)kThreads * U;
+  constexpr int kTile = kThreads * U;
   const int64_t nvec = (n - head) >> 2;
+  const int64_t t = (int64_t)blockIdx.x * kTile;
+  const int64_t left = nvec - t;
   const float4* src[K];
 #pragma unroll
-  for (int k = 0; k < K; ++k) src[k] = reinterpret_cast<const float4*>(in.p[k] + head);
-  float4* dst = reinterpret_cast<float4*>(out + head);
-  const int64_t stride = (int64_t)gridDim.x * kTile;
-  for (int64_t t = (int64_t)blockIdx.x * kTile; t < nvec; t += stride) {
-    const int64_t i0 = t + threadIdx.x;
-    if (t + kTile <= nvec) {
-      float4 v[U][K];
+  for (int k = 0; k < K; ++k) src[k] = reinterpret_cast<const float4*>(in.p[k] + head) + t;
+  float4* dst = reinterpret_cast<float4*>(out + head) + t;
+  if (left >= kTile) {
+    float4 v[U][K];
 #pragma unroll
-      for (int u = 0; u < U; ++u)
+    for (int u = 0; u < U; ++u)
 #pragma unroll
-        for (int k = 0; k < K; ++k) v[u][k] = load_stream(src[k] + i0 + u * kThreads);
+      for (int k = 0; k < K; ++k) v[u][k] = load_stream(src[k] + u * kThreads + threadIdx.x);
 #pragma unroll
-      for (int u = 0; u < U; ++u) store_stream(dst + i0 + u * kThreads, apply4(body, v[u]));
-    } else {
+    for (int u = 0; u < U; ++u) store_stream(dst + u * kThreads + threadIdx.x, apply4(body, v[u]));
+  } else {
+    const int rem = left > 0 ? (int)left : 0;
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t i = i0 + u * kThreads;
-        if (i < nvec) {
-          float4 v[K];
+    for (int u = 0; u < U; ++u) {
+      const int i = u * kThreads + threadIdx.x;
+      if (i < rem) {
+        float4 v[K];
 #pragma unroll
-          for (int k = 0; k < K; ++k) v[k] = load_stream(src[k] + i);
-          store_stream(dst + i, apply4(body, v));
-        }
+        for (int k = 0; k < K; ++k) v[k] = load_stream(src[k] + i);
+        store_stream(dst + i, apply4(body, v));
       }
     }
   }
-  // Ragged edges: threads 0..2 take the head, threads 4..6 the tail (both <= 3).
   if (blockIdx.x == gridDim.x - 1) {
     const int64_t tail0 = head + (nvec << 2);
     const int r = threadIdx.x;
@@ -279,40 +281,47 @@ reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInp
                   typename Op::Acc* __restrict__ partial_out) {
   allow_dependent_launch();
   constexpr int K = Body::kInputs;
-  constexpr int64_t kTile = (int64_t)kThreads * U;
+  constexpr int kTile = kThreads * U;
   using Acc = typename Op::Acc;
   const int64_t nvec = (n - head) >> 2;
+  const int64_t full_tiles = nvec / kTile;
+  const int rem_last = (int)(nvec - full_tiles * kTile);
+  const int64_t grid = gridDim.x;
+  const int64_t b = blockIdx.x;
   const float4* src[K];
 #pragma unroll
-  for (int k = 0; k < K; ++k) src[k] = reinterpret_cast<const float4*>(in.p[k] + head);
+  for (int k = 0; k < K; ++k)
+    src[k] = reinterpret_cast<const float4*>(in.p[k] + head) + b * kTile + threadIdx.x;
+  const int iters = b < full_tiles ? (int)((full_tiles - 1 - b) / grid + 1) : 0;
+  const int64_t stride = grid * kTile;
   Acc acc = Op::init();
-  const int64_t stride = (int64_t)gridDim.x * kTile;
-  for (int64_t t = (int64_t)blockIdx.x * kTile; t < nvec; t += stride) {
-    const int64_t i0 = t + threadIdx.x;
-    if (t + kTile <= nvec) {
-      float4 v[U][K];
+  for (int it = 0; it < iters; ++it) {
+    float4 v[U][K];
 #pragma unroll
-      for (int u = 0; u < U; ++u)
+    for (int u = 0; u < U; ++u)
 #pragma unroll
-        for (int k = 0; k < K; ++k) v[u][k] = load_stream(src[k] + i0 + u * kThreads);
-      float c[U];
+      for (int k = 0; k < K; ++k) v[u][k] = load_stream(src[k] + u * kThreads);
+    float c[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) c[u] = Op::chunk4(apply4(body, v[u]));
-      acc = Op::absorb(acc, fold_chunks<Op, U>(c));
-    } else {
+    for (int u = 0; u < U; ++u) c[u] = Op::chunk4(apply4(body, v[u]));
+    acc = Op::absorb(acc, fold_chunks<Op, U>(c));
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t i = i0 + u * kThreads;
-        if (i < nvec) {
-          float4 v[K];
+    for (int k = 0; k < K; ++k) src[k] += stride;
+  }
+  // The ragged last tile (tile index full_tiles) is the next tile of CTA
+  // full_tiles mod grid, whose pointers now stand at its start.
+  if (rem_last > 0 && b == full_tiles % grid) {
 #pragma unroll
-          for (int k = 0; k < K; ++k) v[k] = load_stream(src[k] + i);
-          acc = Op::absorb(acc, Op::chunk4(apply4(body, v)));
-        }
+    for (int u = 0; u < U; ++u) {
+      if (u * kThreads + (int)threadIdx.x < rem_last) {
+        float4 v[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) v[k] = load_stream(src[k] + u * kThreads);
+        acc = Op::absorb(acc, Op::chunk4(apply4(body, v)));
       }
     }
   }
-  if (blockIdx.x == gridDim.x - 1) {
+  if (b == grid - 1) {
     const int64_t tail0 = head + (nvec << 2);
     const int r = threadIdx.x;
     int64_t i = -1;

@@ -139,7 +139,9 @@ inline int launch_map(float* out, const Ptrs<Body::kInputs>& in, int64_t n, cons
     constexpr int U = MapUnroll<Body::kInputs>::value;
     const int64_t head = head_elems(out, n);
     const int64_t nvec = (n - head) >> 2;
-    const unsigned grid = clamp_grid(ceil_div(nvec, (int64_t)kThreads * U), kMaxGrid);
+    const int64_t tiles = ceil_div(nvec, (int64_t)kThreads * U);
+    if (tiles > kMaxGrid) return LOOM_STATUS_INVALID_ARGUMENT;  // > 2^40 elements: no such GPU
+    const unsigned grid = clamp_grid(tiles, kMaxGrid);
     map_vec_kernel<Body, U><<<grid, kThreads, 0, stream>>>(out, in, n, head, body);
   } else {
     const unsigned grid = clamp_grid(ceil_div(n, (int64_t)kThreads * kScalarUnroll), kMaxGrid);
