@@ -34,10 +34,14 @@ CSRC = Path(__file__).resolve().parent / "csrc"
 CUDA_ARCH = "sm_100a"
 GENCODE = "arch=compute_100a,code=sm_100a"
 
-# Reference optimisation flags that change this backend's output.  Every other
-# flag is accepted and recorded; the B200 plan (always fused, always
-# vectorised, deterministic two-launch reductions) does not depend on it.
-HONOURED_FLAGS = {"cuda-async-wrapper-return"}
+# Reference optimisation flags that change this backend's output: the async
+# wrapper return, and the flags that change how map bodies are rendered (and
+# so their bits).  Every other flag is accepted and recorded; the B200 plan
+# (always fused, always vectorised, deterministic reductions) does not depend
+# on it.
+HONOURED_FLAGS = {"cuda-async-wrapper-return", "cuda-pointwise-tail-tune",
+                  "cuda-pointwise-predicated-select", "cuda-pointwise-selected-tail-plan",
+                  "cuda-body-trait-analysis", "shared-body-trait-analysis"}
 
 
 class BuildError(RuntimeError):
@@ -105,7 +109,8 @@ def load_source_file(path: str) -> List[Program]:
 
 
 def discover_entries(project_root: str, module_filters: Sequence[str] = (),
-                     entry_filters: Sequence[str] = ()) -> List[EntryBundle]:
+                     entry_filters: Sequence[str] = (), enabled: Sequence[str] = ()
+                     ) -> List[EntryBundle]:
     """Collect entries of a project (cuda_backend.ml:158-178, 307-326): every
     ``*.tensor_ir.json`` and every Python module with ``@loom.entry``
     functions below the root, skipping build and hidden dirs, in path order."""
@@ -127,7 +132,7 @@ def discover_entries(project_root: str, module_filters: Sequence[str] = (),
         for prog in load_source_file(path):
             if efilt and prog.entry_name.lower() not in efilt:
                 continue
-            bundles.append(EntryBundle(module, path, prog, plan_entry(prog, module)))
+            bundles.append(EntryBundle(module, path, prog, plan_entry(prog, module, enabled)))
     return bundles
 
 
@@ -326,7 +331,7 @@ def generate_package(project_root: str, out_dir: str, opts: Optional[Options] = 
     opts = opts or Options()
     project_root = os.path.abspath(project_root)
     package = package_name or package_name_of_root(project_root)
-    bundles = discover_entries(project_root, module_filters, entry_filters)
+    bundles = discover_entries(project_root, module_filters, entry_filters, opts.enabled)
     if not bundles:
         raise TensorIRError("no Loom entries matched the requested project selection")
     symbols = [b.plan.symbol for b in bundles]
@@ -365,7 +370,8 @@ def compile_entry(source_file: str, entry_name: str, out_dir: str,
     if not progs:
         raise TensorIRError(f"entry {entry_name!r} not found in {source_file}")
     prog = progs[0]
-    b = EntryBundle(module, os.path.abspath(source_file), prog, plan_entry(prog, module))
+    b = EntryBundle(module, os.path.abspath(source_file), prog,
+                    plan_entry(prog, module, opts.enabled))
     out_dir = os.path.abspath(out_dir)
     header = os.path.join(out_dir, f"{entry_name}_cuda.h")
     source = os.path.join(out_dir, f"{entry_name}_cuda.cu")

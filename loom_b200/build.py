@@ -21,6 +21,12 @@ BUILT_DIR = os.path.join(HERE, "_built")
 SUITE_DIR = os.path.join(BUILT_DIR, "b200_suite")
 
 
+# Reference flags that change how map bodies are rendered; the body-coverage
+# test project is also packaged with them (as frontend_cases_flags).
+RENDER_FLAGS = ["cuda-pointwise-tail-tune", "cuda-pointwise-predicated-select",
+                "cuda-pointwise-selected-tail-plan", "cuda-body-trait-analysis"]
+
+
 def SUITE_OPTIONS() -> artifact.Options:
     """Reference default flags, plus the static-scratch variant of dot."""
     return artifact.Options(noalloc_entries=["dot"])
@@ -56,17 +62,19 @@ def load_suite() -> Package:
     return Package(SUITE_DIR)
 
 
-def build_project(project_dir: str, force: bool = False) -> str:
-    """Package any project into ``loom_b200/_built/<package>/`` (reference
-    default flags) and return that directory; skipped when the library is
-    newer than the project's sources and the backend."""
-    name = artifact.package_name_of_root(project_dir)
-    out = os.path.join(BUILT_DIR, name)
-    lib = os.path.join(out, f"lib{name}.so")
+def build_project(project_dir: str, force: bool = False, enabled=(), name: str = None) -> str:
+    """Package any project into ``loom_b200/_built/<name>/`` (default: the
+    package name) with the given reference flags, and return that directory;
+    skipped when the library is newer than the project's sources and the
+    backend."""
+    pkg = name or artifact.package_name_of_root(project_dir)
+    out = os.path.join(BUILT_DIR, pkg)
+    lib = os.path.join(out, f"lib{pkg}.so")
     newest = _newest_source_mtime()
     for root, _, files in os.walk(project_dir):
         for f in files:
             newest = max(newest, os.path.getmtime(os.path.join(root, f)))
     if force or not os.path.exists(lib) or os.path.getmtime(lib) < newest:
-        artifact.generate_package(project_dir, out, artifact.Options())
+        artifact.generate_package(project_dir, out, artifact.Options(enabled=list(enabled)),
+                                  package_name=pkg)
     return out

@@ -165,9 +165,39 @@ def reduction_family(inputs, scalar_params, body) -> str:
     return "mapped"
 
 
+TRAIT_FLAGS = {"cuda-body-trait-analysis", "shared-body-trait-analysis"}
+
+
+def node_render_flags(enabled, n_inputs: int, scalar_params, body) -> render.RenderFlags:
+    """Rendering switches of one element-wise node under the enabled reference
+    flags (the per-step derivation of src/loom_backend_cuda/cuda_backend.ml:
+    1310-1345; body traits exist only under a trait-analysis flag,
+    src/loom_backend_cuda/cuda_plan.ml:785-792)."""
+    enabled = set(enabled or ())
+    tail = "cuda-pointwise-tail-tune" in enabled
+    pred = "cuda-pointwise-predicated-select" in enabled
+    sel_tail = "cuda-pointwise-selected-tail-plan" in enabled
+    traits = pointwise_traits(n_inputs, scalar_params, body) if enabled & TRAIT_FLAGS else []
+
+    def has(t):
+        return t in traits
+
+    affine_threshold_clamp = has("affine") and has("threshold") and n_inputs == 1
+    affine_clip_threshold = affine_threshold_clamp and has("clip")
+    pred_body = pred and not (sel_tail and affine_clip_threshold) and (
+        affine_threshold_clamp or not (has("threshold") and not has("clip")))
+    return render.RenderFlags(
+        tail_tune=tail,
+        predicated_select=pred_body,
+        fast_divide=sel_tail and has("ratio-book") and not has("branch"),
+        eager_select_then=tail and has("mixed-filter-ratio"),
+    )
+
+
 class _Builder:
-    def __init__(self, prog: Program):
+    def __init__(self, prog: Program, enabled=()):
         self.prog = prog
+        self.enabled = set(enabled)
         self.slots: List[str] = []
         self.blocks: List[NodeBlock] = []
         self.temps: Dict[int, str] = {}
@@ -197,14 +227,20 @@ class _Builder:
         for b in inputs:
             bindings.append((c_ident(b.name), self.value(b.source)))
         self.scalars_used.update(scalar_params)
-        lines = render.render_value_lines(body, c_ident)
+        # Mapped reduction bodies always render with the defaults
+        # (cuda_backend.ml:1071-1085); element-wise nodes take the flags.
+        flags = (node_render_flags(self.enabled, len(inputs), scalar_params, body)
+                 if node_id is not None else render.DEFAULT_FLAGS)
+        lines = render.render_value_lines(body, c_ident, flags=flags)
         temp = f"t{len(self.blocks)}"
         self.blocks.append(NodeBlock(node_id, temp, bindings, lines, body))
         return temp
 
 
-def plan_entry(prog: Program, module_name: str) -> EntryPlan:
-    b = _Builder(prog)
+def plan_entry(prog: Program, module_name: str, enabled=()) -> EntryPlan:
+    """Plan one entry; `enabled` holds the reference optimisation flags (only
+    the body-rendering ones change the generated code)."""
+    b = _Builder(prog, enabled)
     traits: List[str] = []
     family = ""
     if prog.result_kind == "tensor":

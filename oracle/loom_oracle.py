@@ -99,11 +99,59 @@ def _is_bin(e, op=None) -> bool:
     return e["kind"] == "binary" and (op is None or e["op"] == op)
 
 
-def render_expr(e, var) -> str:
-    """render_scalar_expr_with under the default flags (cuda_backend.ml:446-527)."""
-    def r(x):
-        return render_expr(x, var)
+def _soft_threshold(e):
+    """(value, threshold) when e is a soft-threshold select
+    (cuda_backend.ml:365-421), else None."""
+    if e["kind"] != "select" or e["else"]["kind"] != "select":
+        return None
+    outer, inner = e, e["else"]
 
+    def gt(v, t, c):      # v > t, also written t < v
+        return _is_bin(c) and ((c["op"] == "cmpgt" and _eq(c["lhs"], v) and _eq(c["rhs"], t))
+                               or (c["op"] == "cmplt" and _eq(c["lhs"], t) and _eq(c["rhs"], v)))
+
+    def lt_neg(v, t, c):  # v < -t, the negation written -t or 0 - t
+        if not (_is_bin(c, "cmplt") and _eq(c["lhs"], v)):
+            return False
+        m = c["rhs"]
+        return ((m["kind"] == "unary" and m["op"] == "neg" and _eq(m["expr"], t))
+                or (_is_bin(m, "sub") and _is_zero(m["lhs"]) and _eq(m["rhs"], t)))
+
+    def sums(a, b, v, t):
+        return (_eq(a, v) and _eq(b, t)) or (_eq(a, t) and _eq(b, v))
+
+    if _is_bin(outer["then"], "sub") and _is_bin(inner["then"], "add"):
+        v, t = outer["then"]["lhs"], outer["then"]["rhs"]
+        if (gt(v, t, outer["cond"]) and lt_neg(v, t, inner["cond"])
+                and sums(inner["then"]["lhs"], inner["then"]["rhs"], v, t)
+                and _is_zero(inner["else"])):
+            return v, t
+    if _is_bin(outer["then"], "add") and _is_bin(inner["then"], "sub"):
+        v, t = inner["then"]["lhs"], inner["then"]["rhs"]
+        if ((_eq(v, outer["then"]["lhs"]) or _eq(v, outer["then"]["rhs"]))
+                and lt_neg(v, t, outer["cond"]) and gt(v, t, inner["cond"])
+                and sums(outer["then"]["lhs"], outer["then"]["rhs"], v, t)
+                and _is_zero(inner["else"])):
+            return v, t
+    return None
+
+
+def _soft_text(v, t):
+    return f"((({v}) > ({t})) ? (({v}) - ({t})) : ((({v}) < -({t})) ? (({v}) + ({t})) : 0.0f))"
+
+
+def render_expr(e, var, flags=None) -> str:
+    """render_scalar_expr_with (cuda_backend.ml:446-527); `flags` may carry
+    tail_tune (soft-threshold rewrite) and fast_divide."""
+    flags = flags or {}
+
+    def r(x):
+        return render_expr(x, var, flags)
+
+    if flags.get("tail_tune"):
+        st = _soft_threshold(e)
+        if st is not None:
+            return _soft_text(r(st[0]), r(st[1]))
     k = e["kind"]
     if k == "var":
         return var(e["name"])
@@ -126,6 +174,8 @@ def render_expr(e, var) -> str:
         return f"fmaf({r(lhs['lhs'])}, {r(lhs['rhs'])}, -({r(rhs)}))"
     if op == "sub" and _is_bin(rhs, "mul"):
         return f"fmaf(-({r(rhs['lhs'])}), {r(rhs['rhs'])}, {r(lhs)})"
+    if op == "div" and flags.get("fast_divide"):
+        return f"__fdividef({r(lhs)}, {r(rhs)})"
     if op in ("add", "sub", "mul", "div"):
         sym = {"add": "+", "sub": "-", "mul": "*", "div": "/"}[op]
         return f"(({r(lhs)}) {sym} ({r(rhs)}))"
@@ -219,14 +269,29 @@ def _clamp(e):
     return None
 
 
-def value_lines(body, var) -> List[str]:
-    """render_value_lines under the default flags; defines float `value`."""
+def value_lines(body, var, flags=None) -> List[str]:
+    """render_value_lines (cuda_backend.ml:721-848); defines float `value`.
+    `flags`: tail_tune, predicated_select, fast_divide, eager_select_then."""
+    flags = flags or {}
+
+    def R(x):
+        return render_expr(x, var, flags)
+
     clamp = _clamp(body)
     if clamp is not None:
         v, lo, hi = clamp
-        return [f"float value_unclamped = {render_expr(v, var)};",
-                f"float value = fminf(fmaxf(value_unclamped, {render_expr(lo, var)}), "
-                f"{render_expr(hi, var)});"]
+        if flags.get("tail_tune") and not flags.get("predicated_select"):
+            return [f"float value = {R(v)};",
+                    f"if (value < {R(lo)}) value = {R(lo)};",
+                    f"if (value > {R(hi)}) value = {R(hi)};"]
+        return [f"float value_unclamped = {R(v)};",
+                f"float value = fminf(fmaxf(value_unclamped, {R(lo)}), {R(hi)});"]
+    if flags.get("predicated_select"):
+        st = _soft_threshold(body)
+        if st is not None:
+            v, t = R(st[0]), R(st[1])
+            return [f"float value = ((({t}) >= 0.0f) ? copysignf(fmaxf(fabsf({v}) - ({t}), "
+                    f"0.0f), {v}) : ({_soft_text(v, t)}));"]
     if body["kind"] == "select" and _is_bin(body["cond"]) and body["cond"]["op"] in _CMP:
         c = body["cond"]
         # select_reuses_compared_subexpr (cuda_backend.ml:665-684)
@@ -235,10 +300,16 @@ def value_lines(body, var) -> List[str]:
                 guard = "value_guard"
                 o = render_replacing(other, var, reused, guard)
                 lhs, rhs = (guard, o) if on_lhs else (o, guard)
-                return [f"float {guard} = {render_expr(reused, var)};",
+                then_text = render_replacing(body['then'], var, reused, guard)
+                else_text = render_replacing(body['else'], var, reused, guard)
+                if flags.get("eager_select_then"):
+                    return [f"float {guard} = {R(reused)};",
+                            f"float value_candidate = {then_text};",
+                            f"float value = (({lhs}) {_CMP[c['op']]} ({rhs})) ? value_candidate : "
+                            f"({else_text});"]
+                return [f"float {guard} = {R(reused)};",
                         f"float value = (({lhs}) {_CMP[c['op']]} ({rhs})) ? "
-                        f"({render_replacing(body['then'], var, reused, guard)}) : "
-                        f"({render_replacing(body['else'], var, reused, guard)});"]
+                        f"({then_text}) : ({else_text});"]
         # select_reuses_compared_value (cuda_backend.ml:614-645)
         for reused, other, on_lhs in ((c["lhs"], c["rhs"], True), (c["rhs"], c["lhs"], False)):
             if _eq(reused, body["then"]):
@@ -248,19 +319,19 @@ def value_lines(body, var) -> List[str]:
                     fn = "fminf" if on_lhs else "fmaxf"
                 elif c["op"] in ("cmpgt", "cmpge"):
                     fn = "fmaxf" if on_lhs else "fminf"
-                lines = [f"float {sel} = {render_expr(reused, var)};"]
+                lines = [f"float {sel} = {R(reused)};"]
                 if fn is not None and _eq(body["else"], other):
-                    lines.append(f"float value = {fn}({sel}, {render_expr(other, var)});")
+                    lines.append(f"float value = {fn}({sel}, {R(other)});")
                 else:
-                    o = render_expr(other, var)
+                    o = R(other)
                     lhs, rhs = (sel, o) if on_lhs else (o, sel)
                     lines.append(f"float value = (({lhs}) {_CMP[c['op']]} ({rhs})) ? {sel} : "
-                                 f"({render_expr(body['else'], var)});")
+                                 f"({R(body['else'])});")
                 return lines
     if _is_bin(body, "mul") and _eq(body["lhs"], body["rhs"]) and not _is_leaf(body["lhs"]):
-        return [f"float value_factor = {render_expr(body['lhs'], var)};",
+        return [f"float value_factor = {R(body['lhs'])};",
                 "float value = value_factor * value_factor;"]
-    return [f"float value = {render_expr(body, var)};"]
+    return [f"float value = {R(body)};"]
 
 
 # ---------------------------------------------------------------------------
@@ -278,7 +349,54 @@ def _ref(text, params):
     return ("param", text)
 
 
-def entry_c(prog: dict) -> str:
+def _any(e, pred) -> bool:
+    if pred(e):
+        return True
+    k = e["kind"]
+    if k == "unary":
+        return _any(e["expr"], pred)
+    if k == "binary":
+        return _any(e["lhs"], pred) or _any(e["rhs"], pred)
+    if k == "select":
+        return any(_any(e[x], pred) for x in ("cond", "then", "else"))
+    return False
+
+
+def map_node_flags(node: dict, enabled) -> dict:
+    """Rendering switches of one elementwise node under the enabled reference
+    flags: body traits (kernel_plan_common.ml:213-235, computed only under a
+    trait-analysis flag, cuda_plan.ml:785-792) gate them as
+    cuda_backend.ml:1310-1345 does."""
+    enabled = set(enabled or ())
+    body, n_in, scal = node["body"], len(node["inputs"]), list(node["scalar_params"])
+    traits = set()
+    if enabled & {"cuda-body-trait-analysis", "shared-body-trait-analysis"}:
+        branch = _any(body, lambda x: x["kind"] == "select")
+        div = _any(body, lambda x: _is_bin(x, "div"))
+        minmax = _any(body, lambda x: _is_bin(x) and x["op"] in ("min", "max"))
+        addsub = _any(body, lambda x: _is_bin(x) and x["op"] in ("add", "sub"))
+        rules = [(n_in == 1 and bool(scal) and branch, "threshold"),
+                 (n_in == 1 and not scal and (branch or minmax), "simple-activation"),
+                 (n_in == 2 and div and not branch, "ratio-book"),
+                 (n_in == 2 and div and branch, "mixed-filter-ratio"),
+                 (n_in == 1 and branch, "activation-or-threshold"),
+                 (n_in == 2 and branch, "filter-or-book"),
+                 (n_in == 2 and not branch, "affine-vector-update"),
+                 (bool(scal) and addsub, "affine"),
+                 (div, "ratio"), (branch, "branch"), (minmax, "clip")]
+        traits = {name for ok, name in rules if ok}
+    tail = "cuda-pointwise-tail-tune" in enabled
+    pred = "cuda-pointwise-predicated-select" in enabled
+    sel = "cuda-pointwise-selected-tail-plan" in enabled
+    atc = "affine" in traits and "threshold" in traits and n_in == 1
+    return {"tail_tune": tail,
+            "predicated_select": pred and not (sel and atc and "clip" in traits)
+            and (atc or not ("threshold" in traits and "clip" not in traits)),
+            "fast_divide": sel and "ratio-book" in traits and "branch" not in traits,
+            "eager_select_then": tail and "mixed-filter-ratio" in traits}
+
+
+def entry_c(prog: dict, enabled=()) -> str:
     """C for one entry: oracle_<entry>(tensors, scalars, n, out, result, threads)."""
     name = prog["entry_name"]
     params = {p["name"]: p for p in prog["params"]}
@@ -299,16 +417,17 @@ def entry_c(prog: dict) -> str:
             return done[key]
         node = nodes[key]
         assert node["kind"] == "elementwise1d", "a reduction cannot feed a map"
-        return emit_block(node["inputs"], node["body"], f"node_{key}", key)
+        return emit_block(node["inputs"], node["body"], f"node_{key}", key,
+                          map_node_flags(node, enabled))
 
-    def emit_block(inputs, expr, label, key=None) -> str:
+    def emit_block(inputs, expr, label, key=None, flags=None) -> str:
         srcs = [(b["name"], value_of(_ref(b["source"], params))) for b in inputs]
         temp = f"T_{len(done)}_{len(body)}"
         body.append(f"    float {temp};")
         body.append(f"    {{ /* {label} */")
         for nm, src in srcs:
             body.append(f"      const float {_cname(nm)} = {src};")
-        for line in value_lines(expr, _cname):
+        for line in value_lines(expr, _cname, flags):
             body.append("      " + line)
         body.append(f"      {temp} = value;")
         body.append("    }")
@@ -383,10 +502,11 @@ def entry_c(prog: dict) -> str:
     return "\n".join(out)
 
 
-def program_c(programs: Sequence[dict]) -> str:
+def program_c(programs: Sequence[dict], enabled=()) -> str:
     parts = ["/* Generated by oracle/loom_oracle.py -- test infrastructure. */",
+             f"/* reference flags: {', '.join(sorted(enabled)) or 'none'} */",
              "#include <omp.h>", "#include <stdint.h>", '#include "oracle_semantics.h"', ""]
-    parts += [entry_c(p) for p in programs]
+    parts += [entry_c(p, enabled) for p in programs]
     return "\n".join(parts)
 
 
@@ -394,10 +514,10 @@ GCC_FLAGS = ["-O2", "-std=c11", "-fopenmp", "-fPIC", "-shared", "-ffp-contract=o
              "-fno-fast-math", "-fexcess-precision=standard", "-fno-unsafe-math-optimizations"]
 
 
-def build(programs: Sequence[dict], name: str, build_dir: str = BUILD_DIR) -> str:
+def build(programs: Sequence[dict], name: str, build_dir: str = BUILD_DIR, enabled=()) -> str:
     """Write and compile the oracle for `programs`; returns the .so path."""
     os.makedirs(build_dir, exist_ok=True)
-    src = program_c(programs)
+    src = program_c(programs, enabled)
     with open(os.path.join(HERE, "oracle_semantics.h"), "rb") as fh:
         digest = hashlib.sha256(src.encode() + fh.read()).hexdigest()[:12]
     so = os.path.join(build_dir, f"liboracle_{name}_{digest}.so")
@@ -419,9 +539,9 @@ class Oracle:
     """ctypes front of a compiled oracle library."""
 
     def __init__(self, programs: Sequence[dict], name: str = "programs",
-                 build_dir: str = BUILD_DIR):
+                 build_dir: str = BUILD_DIR, enabled=()):
         self.programs = {p["entry_name"]: p for p in programs}
-        self.path = build(list(programs), name, build_dir)
+        self.path = build(list(programs), name, build_dir, enabled)
         self.lib = ctypes.CDLL(self.path)
         self.fns = {}
         for entry in self.programs:

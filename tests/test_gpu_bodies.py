@@ -3,10 +3,18 @@ B200 package -> CUDA) against the oracle: helper functions, clamps, soft
 thresholds, sqrt, exp/log, division, select, negation, a max over a map and
 multi-node chains (tests/golden/sources/cases/frontend_cases.py).
 
+The project is packaged twice: with the reference's default flags, and with
+the flags that change how map bodies are rendered (soft-threshold and
+predicated-select rewrites, the `if` clamp form, `__fdividef` for ratio
+bodies; loom_b200.build.RENDER_FLAGS), each checked against the oracle built
+with the same flags.
+
 Bar: maps and max bit-exact, except `ratio_exp`, whose expf/logf are CUDA's
-(up to 2 ulp / 1 ulp from the correctly rounded value) against the host's
-libm, so it is compared to a relative 1e-6 (about 8 ulp); sums as in
-test_gpu_parity: 1e-6 * max(1, log2 n) * max(|ref|, sqrt(sum v_i^2))."""
+(up to 2 ulp / 1 ulp from the correctly rounded value; with the flags also
+__fdividef, 2 ulp) against the host's libm and IEEE division, so it is
+compared to a relative 1e-6 (about 8 ulp); sums as in test_gpu_parity:
+1e-6 * max(1, log2 n) * max(|ref|, sqrt(sum v_i^2)).
+"""
 
 import math
 import os
@@ -16,7 +24,7 @@ import pytest
 import torch
 
 from loom_b200 import tensor_ir as TI
-from loom_b200.build import build_project
+from loom_b200.build import RENDER_FLAGS, build_project
 from loom_b200.frontend import python_programs
 from loom_b200.loader import Package
 
@@ -30,12 +38,17 @@ SCALARS = {"lo": -0.5, "hi": 0.75, "s": 1.5, "a": 0.3, "t": 0.25}
 SCALARS_BY_ENTRY = {"scaled_chain": {"a": 1.25}}
 
 
-@pytest.fixture(scope="module")
-def cases():
+@pytest.fixture(scope="module", params=["default", "render_flags"])
+def cases(request):
     from oracle.loom_oracle import Oracle
     progs = python_programs(os.path.join(CASES, "frontend_cases.py"))
-    pkg = Package(build_project(CASES))
-    oracle = Oracle([TI.program_to_json(p) for p in progs], name="frontend_cases")
+    if request.param == "default":
+        pkg = Package(build_project(CASES))
+        oracle = Oracle([TI.program_to_json(p) for p in progs], name="frontend_cases")
+    else:
+        pkg = Package(build_project(CASES, enabled=RENDER_FLAGS, name="frontend_cases_flags"))
+        oracle = Oracle([TI.program_to_json(p) for p in progs], name="frontend_cases_flags",
+                        enabled=RENDER_FLAGS)
     return pkg, oracle, {p.entry_name: p for p in progs}
 
 

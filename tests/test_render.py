@@ -108,3 +108,61 @@ def test_two_restatements_agree_on_random_bodies():
     for _ in range(3000):
         body = _random_expr(rng, rng.randint(1, 5), ["x", "y", "a"])
         assert product_lines(body) == oracle_lines(body), body
+
+
+FLAG_SETS = [dict(tail_tune=a, predicated_select=b, fast_divide=c, eager_select_then=d)
+             for a in (False, True) for b in (False, True) for c in (False, True)
+             for d in (False, True)]
+
+
+def _soft(v, t):
+    # x > t ? x - t : (x < -t ? x + t : 0), in both written orders
+    return [T.SSelect(B("cmpgt", v, t), B("sub", v, t),
+                      T.SSelect(B("cmplt", v, T.SUnary("neg", t)), B("add", v, t), C(0.0))),
+            T.SSelect(B("cmplt", v, B("sub", C(0.0), t)), B("add", t, v),
+                      T.SSelect(B("cmplt", t, v), B("sub", v, t), C(0.0)))]
+
+
+def test_flagged_rendering_restatements_agree():
+    rng = random.Random(7)
+    bodies = _soft(V("x"), V("t")) + _soft(B("mul", V("a"), V("x")), V("t"))
+    e = B("add", B("mul", V("a"), V("x")), V("y"))
+    bodies.append(T.SSelect(B("cmpgt", e, C(0.0)), e, C(0.0)))      # guard (eager form)
+    bodies.append(B("div", V("x"), B("add", V("y"), C(1.0))))          # divide
+    bodies += [_random_expr(rng, rng.randint(1, 4), ["x", "y", "a", "t"]) for _ in range(400)]
+    for fl in FLAG_SETS:
+        rf = render.RenderFlags(**fl)
+        for body in bodies:
+            got = render.render_value_lines(body, lambda n: "v_" + n, flags=rf)
+            ref = [re.sub(r"\bu_", "v_", ln) for ln in
+                   O.value_lines(T._expr_to_json(body), lambda n: "u_" + n, fl)]
+            assert got == ref, (fl, body)
+
+
+def test_soft_threshold_forms():
+    body = _soft(V("x"), V("t"))[0]
+    plain = render.render_value_lines(body, lambda n: n)
+    tuned = render.render_value_lines(body, lambda n: n, flags=render.RenderFlags(tail_tune=True))
+    pred = render.render_value_lines(body, lambda n: n,
+                                     flags=render.RenderFlags(predicated_select=True))
+    assert plain != tuned and "copysignf(fmaxf(fabsf(x) - (t), 0.0f), x)" in pred[0]
+
+
+def test_node_flag_derivation_restatements_agree():
+    from loom_b200.plan import node_render_flags
+    rng = random.Random(11)
+    names = ["cuda-pointwise-tail-tune", "cuda-pointwise-predicated-select",
+             "cuda-pointwise-selected-tail-plan", "cuda-body-trait-analysis"]
+    for _ in range(600):
+        n_in = rng.choice([1, 2])
+        ins = ["x", "y"][:n_in]
+        scal = sorted(rng.sample(["a", "t"], rng.randint(0, 2)))
+        body = _random_expr(rng, rng.randint(1, 4), ins + scal)
+        enabled = [f for f in names if rng.random() < 0.6]
+        node = {"body": T._expr_to_json(body), "inputs": [{"name": i} for i in ins],
+                "scalar_params": scal}
+        mine = node_render_flags(enabled, n_in, scal, body)
+        ref = O.map_node_flags(node, enabled)
+        assert (mine.tail_tune, mine.predicated_select, mine.fast_divide,
+                mine.eager_select_then) == (ref["tail_tune"], ref["predicated_select"],
+                                            ref["fast_divide"], ref["eager_select_then"])
