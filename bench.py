@@ -51,6 +51,24 @@ PARAM_NAMES = {
 SCALARS = {"saxpy": {"a": 2.5}, "affine_relu": {"a": 0.75}, "pipeline_sum": {"a": 0.75}}
 MAP_ENTRIES = {"saxpy", "relu", "affine_relu"}
 FALLBACK_HBM_GBS = 6650.0
+_JSON_OUT = None
+
+
+def protect_stdout() -> None:
+    """Send everything written to fd 1 (NCCL prints its version there on
+    rank 0) to stderr, keeping a private copy of stdout for the one JSON
+    line."""
+    global _JSON_OUT
+    if _JSON_OUT is None:
+        sys.stdout.flush()
+        _JSON_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(obj) -> None:
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(obj) + "\n")
+    out.flush()
 
 
 def bytes_per_elem(entry: str) -> int:
@@ -378,7 +396,7 @@ def run_ours(args) -> None:
         }
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline(args.cpu_log2, args.cpu_seconds)
-        print(json.dumps(line), flush=True)
+        emit(line)
     if comm is not None:
         comm.destroy()
     if world > 1:
@@ -503,12 +521,10 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    base = cpu_baseline(args.cpu_log2, args.cpu_seconds)
     # time exactly --steps steps of the bounded sample after --warmup
-    import numpy as np
     from loom_b200 import workloads
     from oracle.loom_oracle import Oracle, load_programs
-    threads = base["cores"]
+    threads = len(os.sched_getaffinity(0))
     oracle = Oracle(load_programs(os.path.join(ROOT, "oracle",
                                                "suite_kernels.tensor_ir.json")), name="b200_suite")
     n = 1 << args.cpu_log2
@@ -523,7 +539,7 @@ def run_reference(args) -> None:
     total = time.perf_counter() - t0
     step_bytes = sum(bytes_per_elem(e) for e in ENTRIES) * n
     value = step_bytes * args.steps / total / 1e9
-    print(json.dumps({
+    emit({
         "impl": "reference",
         "metric": METRIC,
         "value": round(value, 2),
@@ -546,7 +562,7 @@ def run_reference(args) -> None:
                          "sample": f"the 7 suite entries at N=2^{args.cpu_log2} each per step"},
         "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
-    }), flush=True)
+    })
 
 
 def run_pipeline_sweep(args) -> None:
@@ -598,10 +614,10 @@ def run_pipeline_sweep(args) -> None:
         points.append(row)
         del x, y, w, z
         torch.cuda.empty_cache()
-    print(json.dumps({"mode": "pipeline_sweep", "metric": METRIC, "unit": "GB/s",
-                      "config": {"workload": "fused pipeline: affine_relu z = relu(0.75*x + y) "
-                                             "and pipeline_sum s = sum(z*w), x, y, w ~ U(-1,1)"},
-                      "points": points}), flush=True)
+    emit({"mode": "pipeline_sweep", "metric": METRIC, "unit": "GB/s",
+          "config": {"workload": "fused pipeline: affine_relu z = relu(0.75*x + y) "
+                                 "and pipeline_sum s = sum(z*w), x, y, w ~ U(-1,1)"},
+          "points": points})
 
 
 def main():
@@ -620,6 +636,7 @@ def main():
                     help="time the fused pipeline over --sweep sizes instead of the suite step")
     ap.add_argument("--sweep", type=int, nargs="*", default=[10, 14, 18, 22, 26, 30, 32])
     args = ap.parse_args()
+    protect_stdout()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.pipeline_sweep:

@@ -119,3 +119,43 @@ def test_host_side_argument_checks(lib):
     nows.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
     nows.restype = ctypes.c_int
     assert nows(fake, 0, fake) == 0 and nows(fake, -3, fake) == 0  # fast form: n <= 0 is OK
+
+
+def test_multi_gpu_argument_checks(lib):
+    """The multi-GPU entries reject bad arguments before any CUDA or NCCL call."""
+    fake = ctypes.c_void_p(0x10000)
+    multi = lib.loom_kernels_dot_multi
+    multi.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                      ctypes.c_void_p]
+    multi.restype = ctypes.c_int
+    arr = (ctypes.c_void_p * 2)(0x10000, 0x10000)
+    shard = (ctypes.c_int64 * 2)(16, 16)
+    assert multi(0, arr, arr, arr, shard, arr, arr, arr, None) == 1       # no devices
+    assert multi(25, arr, arr, arr, shard, arr, arr, arr, None) == 1      # > 24 ranks
+    assert multi(2, None, arr, arr, shard, arr, arr, arr, None) == 1      # no communicators
+    nulls = (ctypes.c_void_p * 2)(0x10000, None)
+    assert multi(2, arr, nulls, arr, shard, arr, arr, arr, None) == 1    # null shard input
+    bad = (ctypes.c_int64 * 2)(16, -1)
+    assert multi(2, arr, arr, arr, bad, arr, arr, arr, None) == 1        # negative shard
+    sizes = (ctypes.c_size_t * 2)(8, 8)
+    assert multi(2, arr, arr, arr, shard, arr, arr, sizes, None) == 2    # workspace too small
+    dist = lib.loom_kernels_dot_dist
+    dist.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p,
+                     ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
+    dist.restype = ctypes.c_int
+    assert dist(fake, fake, -1, fake, fake, 1 << 20, fake, None) == 1     # n_local < 0
+    assert dist(fake, fake, 16, fake, fake, 1 << 20, None, None) == 1     # no communicator
+    assert dist(fake, fake, 16, fake, fake, 8, fake, None) == 2           # workspace too small
+    rdist = lib.loom_kernels_relu_dist
+    rdist.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+                      ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p]
+    rdist.restype = ctypes.c_int
+    assert rdist(None, 0, None, None, 0, None, None) == 0                 # empty map shard
+    init = lib.loom_b200_suite_comm_init_rank
+    init.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t]
+    init.restype = ctypes.c_int
+    handle = ctypes.c_void_p(0)
+    assert init(ctypes.byref(handle), 2, 2, fake, 128) == 1               # rank out of range
+    assert init(ctypes.byref(handle), 0, 0, fake, 128) == 1               # no ranks
+    assert init(ctypes.byref(handle), 2, 0, fake, 4) == 1                 # id too short
