@@ -16,6 +16,12 @@ synchronous `loom_kernels_<entry>` call) with pinned HOST buffers: every
 step copies each entry's inputs host->device, calls the entry, and copies the
 result back.
 
+`reference_kernels` (1 GPU) times, on the same inputs and GPU, the CUDA that
+the reference's backend generates for the same seven entries, restated by
+hand for two of its optimisation profiles (baseline/loom_reference_style.cu):
+"none" (no passes: unfused, scalar, tree reductions with a host combine loop)
+and "cuda" (its full CUDA set: fused, float4 maps, atomic-output sums).
+
 `--impl reference` times the reference's CPU semantics for the same workload
 on this machine's host cores (the C oracle: the reference has no CPU
 implementation of this path and its OCaml compiler cannot be built here),
@@ -334,6 +340,9 @@ def run_ours(args) -> None:
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(pkg, data, outs, n, args, world, comm)
+    ref_kernels = None
+    if world == 1 and args.ref_kernel_steps > 0:
+        ref_kernels = run_reference_kernels(data, outs, n, args)
     all_clocks = gather_obj(world, clocks)
     all_kernels = gather_obj(world, kernel_ms)
 
@@ -394,6 +403,10 @@ def run_ours(args) -> None:
             "gpu_launches": args.steps * sum(launches_per_call(e, world) for e in ENTRIES),
             "e2e": e2e,
         }
+        if ref_kernels is not None:
+            ref_kernels["product_over_profile"] = {
+                p: round(value / v["value"], 3) for p, v in ref_kernels["profiles"].items()}
+            line["reference_kernels"] = ref_kernels
         if world == 1 and not args.no_cpu:
             line["cpu_baseline"] = cpu_baseline(args.cpu_log2, args.cpu_seconds)
         emit(line)
@@ -486,6 +499,77 @@ def run_e2e(pkg, data, outs, n, args, world, comm):
                          "path": ("loom_kernels_<entry> (synchronous reference ABI)"
                                   if world == 1 else "loom_kernels_<entry>_dist")
                                  + ", one whole-array copy in and out"}}
+
+
+def run_reference_kernels(data, outs, n, args):
+    """The reference's generated CUDA for the same seven entries, restated by
+    hand (baseline/loom_reference_style.cu) under its "none" and "cuda"
+    profiles, timed on this GPU like the product: CUDA events around every
+    call on the launching stream, the same inputs, steps of the seven calls.
+    Each profile's outputs are checked against the product's first."""
+    import torch
+    from baseline import reference_style as rs
+    lib = rs.ReferenceStyle()
+    stream = torch.cuda.current_stream()
+    step_bytes = sum(bytes_per_elem(e) for e in ENTRIES) * n
+    result = {"source": "baseline/loom_reference_style.cu (nvcc -O3, sm_100a)",
+              "steps": args.ref_kernel_steps, "profiles": {}}
+    for profile in rs.PROFILES:
+        calls, bufs = [], []
+        for e in ENTRIES:
+            kw = {p: data[t] for p, t in zip(PARAM_NAMES[e], TENSORS[e])}
+            kw.update(SCALARS.get(e, {}))
+            out = torch.empty_like(outs[e])
+            size = lib.workspace_size(profile, e, n)
+            ws = torch.empty(size, dtype=torch.uint8, device="cuda") if size else None
+            bufs.append((out, ws))
+            calls.append((e, out, lib.bind(profile, e, n, out, ws, **kw)))
+
+        def step(events=None):
+            for i, (e, _, fn) in enumerate(calls):
+                if events is not None:
+                    events[i][0].record(stream)
+                st = fn()
+                if st != 0:
+                    raise RuntimeError(f"reference-style {profile} {e} returned status {st}")
+                if events is not None:
+                    events[i][1].record(stream)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        agrees = {}
+        for e, out, _ in calls:
+            if e in MAP_ENTRIES or e == "max_value":
+                agrees[e] = bool(torch.equal(out.view(torch.int32), outs[e].view(torch.int32)))
+            else:
+                a, b = float(out[0]), float(outs[e][0])
+                agrees[e] = abs(a - b) <= 1e-4 * (abs(b) + math.sqrt(n))
+        ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in calls] for _ in range(args.ref_kernel_steps)]
+        start = torch.cuda.Event(enable_timing=True)
+        end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(stream)
+        for s in range(args.ref_kernel_steps):
+            step(ev[s])
+        end.record(stream)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / args.ref_kernel_steps
+        kernels = {}
+        for i, (e, _, _) in enumerate(calls):
+            k_ms = sum(ev[s][i][0].elapsed_time(ev[s][i][1])
+                       for s in range(args.ref_kernel_steps)) / args.ref_kernel_steps
+            kernels[e] = {"us_per_call": round(k_ms * 1e3, 2),
+                          "gbs": round(bytes_per_elem(e) * n / (k_ms * 1e-3) / 1e9, 1)}
+        result["profiles"][profile] = {
+            "value": round(step_bytes / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(ms, 4),
+            "gpu_launches_per_step": sum(rs.LAUNCHES_2P28[profile].values()),
+            "kernels": kernels, "agrees_with_product": agrees}
+        del calls, bufs
+        torch.cuda.empty_cache()
+    return result
 
 
 def cpu_baseline(log2n: int, seconds: float, threads: int = 0):
@@ -630,6 +714,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ref-kernel-steps", type=int, default=30,
+                    help="steps of the reference-style GPU kernels (1 GPU; 0 skips them)")
     ap.add_argument("--cpu-log2", type=int, default=24)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--pipeline-sweep", action="store_true",

@@ -47,7 +47,7 @@ namespace loomb {
 constexpr int kThreads = 256;            // threads per streaming CTA
 constexpr int kFinalizeThreads = 1024;   // threads of the one-CTA finalize
 constexpr int kScalarUnroll = 8;         // 32-bit elements per thread per tile (scalar path)
-constexpr int kMaxPartials = 65536;      // upper bound on reduction CTAs (fp64 partial slots)
+constexpr int kMaxPartials = 32768;      // upper bound on reduction CTAs (fp64 partial slots)
 constexpr int64_t kMinTileElems = (int64_t)kThreads * 4;  // smallest tile of any kernel
 constexpr int64_t kMaxGrid = (int64_t)1 << 30;
 constexpr int kMaxDevices = 64;
@@ -375,8 +375,10 @@ reduce_scalar_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::k
   store_reduction<Op>(acc, partials, out, partial_out);
 }
 
-// One CTA folds `count` CTA partials in a fixed order (four interleaved
-// accumulators per thread, then the CTA tree).  Writes the fp32 result to
+// One CTA folds `count` CTA partials in a fixed order: each thread issues 16
+// independent loads per round (the partials are in L2, so the fold is bound
+// by load latency, not bandwidth) into four interleaved accumulators, then
+// the CTA tree.  Writes the fp32 result to
 // `out` (if non-null) and the full-precision value to `partial_out` (if
 // non-null; the multi-GPU path all-gathers it).
 template <class Op>
@@ -386,16 +388,18 @@ reduce_finalize_kernel(const typename Op::Acc* __restrict__ partials, const int 
   using Acc = typename Op::Acc;
   constexpr int T = kFinalizeThreads;
   wait_for_prerequisite_grid();  // no-op unless launched as a programmatic dependent
-  Acc a0 = Op::init(), a1 = Op::init(), a2 = Op::init(), a3 = Op::init();
+  constexpr int kLoads = 16;
+  Acc a[4] = {Op::init(), Op::init(), Op::init(), Op::init()};
   int i = threadIdx.x;
-  for (; i + 3 * T < count; i += 4 * T) {
-    a0 = Op::combine(a0, partials[i]);
-    a1 = Op::combine(a1, partials[i + T]);
-    a2 = Op::combine(a2, partials[i + 2 * T]);
-    a3 = Op::combine(a3, partials[i + 3 * T]);
+  for (; i + (kLoads - 1) * T < count; i += kLoads * T) {
+    Acc v[kLoads];
+#pragma unroll
+    for (int j = 0; j < kLoads; ++j) v[j] = partials[i + j * T];
+#pragma unroll
+    for (int j = 0; j < kLoads; ++j) a[j & 3] = Op::combine(a[j & 3], v[j]);
   }
-  for (; i < count; i += T) a0 = Op::combine(a0, partials[i]);
-  Acc acc = Op::combine(Op::combine(a0, a1), Op::combine(a2, a3));
+  for (; i < count; i += T) a[0] = Op::combine(a[0], partials[i]);
+  Acc acc = Op::combine(Op::combine(a[0], a[1]), Op::combine(a[2], a[3]));
   acc = block_reduce<Op, T>(acc);
   if (threadIdx.x == 0) {
     if (out != nullptr) out[0] = Op::to_float(acc);
