@@ -8,8 +8,10 @@
                                 [--enable-opt FLAG ...]
 
 Entries are read from ``*.tensor_ir.json`` files (the TensorIR the reference
-front end dumps with ``--emit tensor-ir``); ``--cuda-arch`` is accepted for
-compatibility and must name sm_100a.
+front end dumps with ``--emit tensor-ir``) and from Python modules written in
+the reference's entry language (``loom.entry`` functions, lowered by
+``loom_b200.frontend``); ``--cuda-arch`` is accepted for compatibility and
+must name sm_100a.
 """
 
 from __future__ import annotations
