@@ -595,10 +595,23 @@ def cpu_baseline(log2n: int, seconds: float, threads: int = 0):
         if total >= seconds:
             break
     step_bytes = sum(bytes_per_elem(e) for e in ENTRIES) * n
+    # the same sample on one core, for about a quarter of the time
+    reps1 = 0
+    t0 = time.perf_counter()
+    while True:
+        for e in ENTRIES:
+            oracle.run(e, inputs[e], threads=1)
+        reps1 += 1
+        total1 = time.perf_counter() - t0
+        if total1 >= seconds / 4:
+            break
     return {"value": round(step_bytes * reps / total / 1e9, 2), "unit": "GB/s",
             "cores": threads, "kind": "port",
             "sample": f"the 7 suite entries at N=2^{log2n} each, {reps} steps in {total:.1f} s",
-            "seconds": round(total, 2)}
+            "seconds": round(total, 2),
+            "single_thread": {"value": round(step_bytes * reps1 / total1 / 1e9, 2),
+                              "unit": "GB/s", "cores": 1,
+                              "sample": f"{reps1} steps in {total1:.1f} s"}}
 
 
 def run_reference(args) -> None:
@@ -649,18 +662,78 @@ def run_reference(args) -> None:
     })
 
 
+def _median_us(call, reps: int, flush, stream) -> float:
+    """Median device time of `call` in us: CUDA events on the launching
+    stream around each call, after 3 untimed calls.  `flush` is None or a
+    pair of buffers larger than L2: before every timed call the first is
+    rewritten (so no input is served from L2) and the second is read, which
+    writes the dirty lines of the first back before the timed call starts
+    rather than during it."""
+    import torch
+    for _ in range(3):
+        call()
+    times = []
+    for _ in range(reps):
+        if flush is not None:
+            flush[0].fill_(1.0)
+            flush[1].sum()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        call()
+        b.record(stream)
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    return statistics.median(times)
+
+
+def _reference_calls(lib, entry, n, out, kw):
+    """Bound reference-style calls of both profiles, with their workspaces."""
+    import torch
+    calls = {}
+    for profile in ("cuda", "none"):
+        size = lib.workspace_size(profile, entry, n)
+        ws = torch.empty(size, dtype=torch.uint8, device="cuda") if size else None
+        fn = lib.bind(profile, entry, n, out, ws, **kw)
+
+        def call(fn=fn, profile=profile):
+            st = fn()
+            if st != 0:
+                raise RuntimeError(f"reference-style {profile} {entry} returned status {st}")
+        calls[profile] = (call, ws)
+    return calls
+
+
+def _timed_row(row, entry, nbytes, product_call, ref_calls, reps, flush, stream, peak):
+    us = _median_us(product_call, reps, flush, stream)
+    row[entry + "_us"] = round(us, 2)
+    row[entry + "_gbs"] = round(nbytes / (us * 1e-6) / 1e9, 1)
+    row[entry + "_frac"] = round(nbytes / (us * 1e-6) / 1e9 / peak, 4)
+    for profile, (call, _) in ref_calls.items():
+        r_us = _median_us(call, reps, flush, stream)
+        row[f"{entry}_ref_{profile}_us"] = round(r_us, 2)
+        row[f"{entry}_ref_{profile}_gbs"] = round(nbytes / (r_us * 1e-6) / 1e9, 1)
+
+
 def run_pipeline_sweep(args) -> None:
     """The fused-pipeline configuration swept over N (1 GPU): device time per
     call of affine_relu (z = relu(a*x + y)) and pipeline_sum (sum(z*w)),
-    median of CUDA-event-timed calls; for N*12 bytes below 512 MiB a 512 MiB
-    buffer is rewritten before every timed call so that no input is served
-    from L2.  Prints one JSON line."""
+    median of CUDA-event-timed calls, for the product and for the
+    reference-style kernels of both profiles on the same inputs.  A 512 MiB
+    buffer is rewritten (then another read) before every timed call, so
+    that no input is served from L2 and the kernels' cache hints cannot
+    favour one side through lines left over from the previous call.  Every call is bound once, so
+    the per-call host work is the same for both.  Prints one JSON line."""
     import torch
+    from baseline.reference_style import ReferenceStyle
     from loom_b200.build import load_suite
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     pkg = load_suite()
+    lib = ReferenceStyle()
+    peak, peak_src = read_peak()
     stream = torch.cuda.current_stream()
-    flush = torch.empty(128 << 20, dtype=torch.float32, device="cuda")
+    flush_buf = (torch.empty(128 << 20, dtype=torch.float32, device="cuda"),
+                 torch.ones(128 << 20, dtype=torch.float32, device="cuda"))
     points = []
     gen = torch.Generator(device="cuda")
     for log2n in args.sweep:
@@ -672,36 +745,72 @@ def run_pipeline_sweep(args) -> None:
         z = torch.empty(n, device="cuda")
         s = torch.empty(1, device="cuda")
         reps = 200 if n <= (1 << 22) else (20 if n <= (1 << 28) else 5)
-        needs_flush = 12 * n < (512 << 20)
-        row = {"n": n, "log2n": log2n, "l2_flush": needs_flush}
-        for entry, call, nbytes in (
-                ("affine_relu", lambda: pkg["affine_relu"](out=z, stream=stream, x=x, y=y, a=0.75),
-                 12 * n),
-                ("pipeline_sum", lambda: pkg["pipeline_sum"](out=s, stream=stream, x=x, y=y, w=w,
-                                                             a=0.75), 12 * n)):
-            for _ in range(3):
-                call()
-            times = []
-            for _ in range(reps):
-                if needs_flush:
-                    flush.fill_(1.0)
-                a = torch.cuda.Event(enable_timing=True)
-                b = torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                call()
-                b.record(stream)
-                b.synchronize()
-                times.append(a.elapsed_time(b) * 1e3)
-            us = statistics.median(times)
-            row[entry + "_us"] = round(us, 2)
-            row[entry + "_gbs"] = round(nbytes / (us * 1e-6) / 1e9, 1)
+        flush = flush_buf
+        row = {"n": n, "log2n": log2n, "l2_flush": True}
+        kz = {"a": 0.75, "x": x, "y": y}
+        ks = {"a": 0.75, "x": x, "y": y, "w": w}
+        refs = _reference_calls(lib, "affine_relu", n, z, kz)
+        call, _ = pkg["affine_relu"].bind(out=z, stream=stream, **kz)
+        _timed_row(row, "affine_relu", 12 * n, call, refs, reps, flush, stream, peak)
+        del refs
+        refs = _reference_calls(lib, "pipeline_sum", n, s, ks)
+        call, _ = pkg["pipeline_sum"].bind(out=s, stream=stream, **ks)
+        _timed_row(row, "pipeline_sum", 12 * n, call, refs, reps, flush, stream, peak)
+        del refs
         points.append(row)
         del x, y, w, z
         torch.cuda.empty_cache()
-    emit({"mode": "pipeline_sweep", "metric": METRIC, "unit": "GB/s",
+    emit({"mode": "pipeline_sweep", "metric": METRIC, "unit": "GB/s", "peak": peak,
+          "peak_source": peak_src,
           "config": {"workload": "fused pipeline: affine_relu z = relu(0.75*x + y) "
                                  "and pipeline_sum s = sum(z*w), x, y, w ~ U(-1,1)"},
           "points": points})
+
+
+# The four single-entry workload configurations, each at its own size.
+CONFIG_POINTS = [("saxpy", 24), ("relu", 26), ("dot", 28), ("l2_norm_sq", 30), ("max_value", 30)]
+
+
+def run_config_sweep(args) -> None:
+    """Each workload configuration at its own N (saxpy 2^24, relu 2^26, dot
+    2^28, l2_norm_sq and max_value 2^30; 1 GPU): median device time per call
+    of the product and of the reference-style kernels of both profiles, on
+    the configuration's seeded inputs.  A 512 MiB buffer is rewritten (then
+    another read) before every timed call.  Prints one JSON line."""
+    import torch
+    from baseline.reference_style import ReferenceStyle
+    from loom_b200.build import load_suite
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    pkg = load_suite()
+    lib = ReferenceStyle()
+    peak, peak_src = read_peak()
+    stream = torch.cuda.current_stream()
+    flush_buf = (torch.empty(128 << 20, dtype=torch.float32, device="cuda"),
+                 torch.ones(128 << 20, dtype=torch.float32, device="cuda"))
+    points = []
+    for entry, log2n in CONFIG_POINTS:
+        n = 1 << log2n
+        data = make_inputs(n, 0)
+        kw = {p: data[t] for p, t in zip(PARAM_NAMES[entry], TENSORS[entry])}
+        kw.update(SCALARS.get(entry, {}))
+        for k in list(data):
+            if k not in TENSORS[entry]:
+                del data[k]
+        torch.cuda.empty_cache()
+        out = torch.empty(n if entry in MAP_ENTRIES else 1, device="cuda")
+        nbytes = bytes_per_elem(entry) * n
+        flush = flush_buf
+        reps = 50 if n <= (1 << 26) else 20
+        row = {"entry": entry, "n": n, "log2n": log2n, "l2_flush": True,
+               "bytes_per_call": nbytes}
+        refs = _reference_calls(lib, entry, n, out, kw)
+        call, _ = pkg[entry].bind(out=out, stream=stream, **kw)
+        _timed_row(row, entry, nbytes, call, refs, reps, flush, stream, peak)
+        points.append(row)
+        del refs, data, kw, out
+        torch.cuda.empty_cache()
+    emit({"mode": "config_sweep", "metric": METRIC, "unit": "GB/s", "peak": peak,
+          "peak_source": peak_src, "points": points})
 
 
 def main():
@@ -721,10 +830,15 @@ def main():
     ap.add_argument("--pipeline-sweep", action="store_true",
                     help="time the fused pipeline over --sweep sizes instead of the suite step")
     ap.add_argument("--sweep", type=int, nargs="*", default=[10, 14, 18, 22, 26, 30, 32])
+    ap.add_argument("--config-sweep", action="store_true",
+                    help="time each single-entry configuration at its own N instead of the step")
     args = ap.parse_args()
     protect_stdout()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.config_sweep:
+        run_config_sweep(args)
+        return
     if args.pipeline_sweep:
         run_pipeline_sweep(args)
     elif args.impl == "reference":

@@ -38,6 +38,7 @@
 //    grid.  Max keeps fp32 fmaxf throughout (exact in any order).
 #pragma once
 
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -51,6 +52,7 @@ constexpr int kMaxPartials = 32768;      // upper bound on reduction CTAs (fp64 
 constexpr int64_t kMinTileElems = (int64_t)kThreads * 4;  // smallest tile of any kernel
 constexpr int64_t kMaxGrid = (int64_t)1 << 30;
 constexpr int kMaxDevices = 64;
+constexpr int kMaxClusterCtas = 8;       // portable thread-block cluster size
 
 // float4 loads per input per thread per tile (measured best on B200).
 template <int K>
@@ -259,12 +261,35 @@ __device__ __forceinline__ void wait_for_prerequisite_grid() {
 }
 
 // A one-CTA reduction is already complete in that CTA: it writes the result
-// itself and the launcher skips the finalize kernel.
-template <class Op>
+// itself and the launcher skips the finalize kernel.  With kCluster the whole
+// grid (at most kMaxClusterCtas CTAs) is one thread-block cluster: each CTA
+// leaves its value in its shared memory, and CTA rank 0 folds them in rank
+// order through distributed shared memory, so a small reduction is complete
+// in one launch.  The second cluster barrier keeps every CTA's shared memory
+// alive until rank 0 has read it.  `acc` is valid in thread 0 only.
+template <class Op, bool kCluster>
 __device__ __forceinline__ void store_reduction(typename Op::Acc acc,
                                                 typename Op::Acc* __restrict__ partials,
                                                 float* __restrict__ out,
                                                 typename Op::Acc* __restrict__ partial_out) {
+  using Acc = typename Op::Acc;
+  if constexpr (kCluster) {
+    namespace cg = cooperative_groups;
+    __shared__ Acc cta_value;
+    cg::cluster_group cluster = cg::this_cluster();
+    if (threadIdx.x == 0) cta_value = acc;
+    cluster.sync();
+    if (threadIdx.x == 0 && cluster.block_rank() == 0) {
+      Acc total = acc;
+      const unsigned ctas = cluster.num_blocks();
+      for (unsigned r = 1; r < ctas; ++r)
+        total = Op::combine(total, *cluster.map_shared_rank(&cta_value, r));
+      if (out != nullptr) out[0] = Op::to_float(total);
+      if (partial_out != nullptr) partial_out[0] = total;
+    }
+    cluster.sync();
+    return;
+  }
   if (threadIdx.x != 0) return;
   if (gridDim.x == 1) {
     if (out != nullptr) out[0] = Op::to_float(acc);
@@ -274,7 +299,7 @@ __device__ __forceinline__ void store_reduction(typename Op::Acc acc,
   }
 }
 
-template <class Op, class Body, int U>
+template <class Op, class Body, int U, bool kCluster = false>
 __global__ void __launch_bounds__(kThreads)
 reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInputs> in,
                   const int64_t n, const int64_t head, const Body body, float* __restrict__ out,
@@ -330,7 +355,7 @@ reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInp
     if (i >= 0) acc = Op::absorb(acc, apply1(body, in, i));
   }
   acc = block_reduce<Op>(acc);
-  store_reduction<Op>(acc, partials, out, partial_out);
+  store_reduction<Op, kCluster>(acc, partials, out, partial_out);
 }
 
 template <class Op, class Body>
@@ -372,7 +397,7 @@ reduce_scalar_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::k
     }
   }
   acc = block_reduce<Op>(acc);
-  store_reduction<Op>(acc, partials, out, partial_out);
+  store_reduction<Op, false>(acc, partials, out, partial_out);
 }
 
 // One CTA folds `count` CTA partials in a fixed order: each thread issues 16

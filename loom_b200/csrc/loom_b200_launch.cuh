@@ -6,8 +6,8 @@
 // :2344-2422): instead of fixed block-count caps (4096 / 32768 blocks of 256
 // threads) and a host loop of combine launches, every kernel gets one CTA per
 // tile (a reduction at most kMaxPartials CTAs, or fewer when the caller's
-// scratch has fewer partial slots), and a reduction is always exactly two
-// launches.
+// scratch has fewer partial slots), and a reduction is one launch when its
+// grid fits one thread-block cluster (at most 8 CTAs) and two otherwise.
 //
 // Nothing here allocates device memory and nothing holds device state.
 #pragma once
@@ -123,6 +123,35 @@ inline int launch_finalize(const typename Op::Acc* partials, int count, float* o
   return launch_status();
 }
 
+// A grid of 2..kMaxClusterCtas CTAs launched as one thread-block cluster:
+// the CTAs fold their values through distributed shared memory, so the
+// reduction needs no finalize launch.  Returns false (with the error
+// cleared) where the cluster launch is refused; the caller then takes the
+// two-launch path.
+template <class Op, class Body, int U>
+inline bool launch_cluster_reduce(unsigned grid, const Ptrs<Body::kInputs>& in, int64_t n,
+                                  int64_t head, const Body& body, float* out,
+                                  typename Op::Acc* partial_out, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = grid;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  typename Op::Acc* no_partials = nullptr;
+  if (cudaLaunchKernelEx(&cfg, reduce_vec_kernel<Op, Body, U, true>, no_partials, in, n, head,
+                         body, out, partial_out) == cudaSuccess)
+    return true;
+  cudaGetLastError();
+  return false;
+}
+
 inline unsigned clamp_grid(int64_t g, int64_t cap) {
   if (g > cap) g = cap;
   if (g < 1) g = 1;
@@ -165,6 +194,9 @@ inline int launch_reduce(const Ptrs<Body::kInputs>& in, int64_t n, const Body& b
     const int64_t head = head_elems(in.p[0], n);
     const int64_t nvec = (n - head) >> 2;
     grid = clamp_grid(ceil_div(nvec, (int64_t)kThreads * U), max_partials);
+    if (grid > 1 && grid <= (unsigned)kMaxClusterCtas &&
+        launch_cluster_reduce<Op, Body, U>(grid, in, n, head, body, out, partial_out, stream))
+      return LOOM_STATUS_OK;
     reduce_vec_kernel<Op, Body, U><<<grid, kThreads, 0, stream>>>(partials, in, n, head, body,
                                                                    out, partial_out);
   } else {

@@ -150,6 +150,31 @@ class Entry:
             raise LoomError(self.symbol, status)
         return out
 
+    def bind(self, out=None, stream=None, **inputs):
+        """The same call with every argument converted once: returns
+        `(call, out)`, where `call()` launches on `stream` (the legacy
+        default stream when None) and raises LoomError on a bad status.
+        For launch loops where the per-call Python work would show, and for
+        stream capture.  The tensors must stay alive while `call` is used."""
+        n = self._n(inputs)
+        device = inputs[self.tensor_params[0]].device
+        if out is None:
+            out = self.new_output(n, device)
+        args = self._args(inputs, n)
+        ws = self.workspace(n, device)
+        wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
+        wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
+        handle = getattr(stream, "cuda_stream", stream) if stream is not None else 0
+        full = args + [ctypes.c_int64(n), ctypes.c_void_p(out.data_ptr()), wsp, wss,
+                       ctypes.c_void_p(handle)]
+        fn, symbol = self.stream_fn, self.symbol
+
+        def call():
+            status = fn(*full)
+            if status != 0:
+                raise LoomError(symbol, status)
+        return call, out
+
     def call_raw(self, *args) -> int:
         return int(self.fn(*args))
 

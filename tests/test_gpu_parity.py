@@ -180,3 +180,16 @@ def test_status_codes_on_device(suite_pkg):
                       ctypes.c_size_t(ws.numel())) == 0
     m = suite_pkg["relu"]
     assert m.call_raw(p(x), ctypes.c_int64(0), p(out), None, ctypes.c_size_t(0)) == 0
+
+
+@pytest.mark.parametrize("entry", ["saxpy", "dot", "max_value"])
+def test_bound_call_matches_plain_call(suite_pkg, entry):
+    n = 4099
+    inp = workloads.entry_inputs(entry, n, seed_offset=5)
+    dev = {k: (to_device(v) if isinstance(v, np.ndarray) else v) for k, v in inp.items()}
+    want = suite_pkg[entry](**dev).cpu().numpy()
+    call, out = suite_pkg[entry].bind(stream=torch.cuda.current_stream(), **dev)
+    for _ in range(2):
+        call()
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
