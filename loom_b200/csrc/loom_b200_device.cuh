@@ -77,6 +77,20 @@ __device__ __forceinline__ float load_stream(const float* p) { return __ldcs(p);
 __device__ __forceinline__ void store_stream(float4* p, const float4& v) { __stcs(p, v); }
 __device__ __forceinline__ void store_stream(float* p, float v) { __stcs(p, v); }
 
+// Programmatic dependent launch.  Every kernel here is launched as a
+// programmatic dependent of the kernel before it on the stream.  It first
+// lets its own dependent be scheduled (launch_dependents), then waits for
+// its prerequisite grid to complete and its writes to become visible
+// (wait) before it touches global memory.  Both are no-ops for a kernel
+// launched without the attribute.
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void wait_for_prerequisite_grid() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 template <class Body>
 __device__ __forceinline__ float4 apply4(const Body& body, const float4 (&v)[Body::kInputs]) {
   constexpr int K = Body::kInputs;
@@ -119,6 +133,8 @@ template <class Body, int U>
 __global__ void __launch_bounds__(kThreads)
 map_vec_kernel(float* __restrict__ out, const Ptrs<Body::kInputs> in, const int64_t n,
                const int64_t head, const Body body) {
+  allow_dependent_launch();
+  wait_for_prerequisite_grid();
   constexpr int K = Body::kInputs;
   constexpr int kTile = kThreads * U;
   const int64_t nvec = (n - head) >> 2;
@@ -164,6 +180,8 @@ template <class Body>
 __global__ void __launch_bounds__(kThreads)
 map_scalar_kernel(float* __restrict__ out, const Ptrs<Body::kInputs> in, const int64_t n,
                   const Body body) {
+  allow_dependent_launch();
+  wait_for_prerequisite_grid();
   constexpr int kU = kScalarUnroll;
   constexpr int64_t kTile = (int64_t)kThreads * kU;
   const int64_t stride = (int64_t)gridDim.x * kTile;
@@ -249,16 +267,6 @@ __device__ __forceinline__ float fold_chunks(const float (&c)[U]) {
   }
 }
 
-// Lets the finalize kernel, launched as a programmatic dependent of this
-// grid, be scheduled early; it still waits (griddepcontrol.wait) for this
-// whole grid to complete and its writes to be visible before reading.
-__device__ __forceinline__ void allow_dependent_launch() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-__device__ __forceinline__ void wait_for_prerequisite_grid() {
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
 
 // A one-CTA reduction is already complete in that CTA: it writes the result
 // itself and the launcher skips the finalize kernel.  With kCluster the whole
@@ -305,6 +313,7 @@ reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInp
                   const int64_t n, const int64_t head, const Body body, float* __restrict__ out,
                   typename Op::Acc* __restrict__ partial_out) {
   allow_dependent_launch();
+  wait_for_prerequisite_grid();
   constexpr int K = Body::kInputs;
   constexpr int kTile = kThreads * U;
   using Acc = typename Op::Acc;
@@ -364,6 +373,7 @@ reduce_scalar_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::k
                      const int64_t n, const Body body, float* __restrict__ out,
                      typename Op::Acc* __restrict__ partial_out) {
   allow_dependent_launch();
+  wait_for_prerequisite_grid();
   using Acc = typename Op::Acc;
   constexpr int kU = kScalarUnroll;
   constexpr int64_t kTile = (int64_t)kThreads * kU;
@@ -412,7 +422,8 @@ reduce_finalize_kernel(const typename Op::Acc* __restrict__ partials, const int 
                        float* __restrict__ out, typename Op::Acc* __restrict__ partial_out) {
   using Acc = typename Op::Acc;
   constexpr int T = kFinalizeThreads;
-  wait_for_prerequisite_grid();  // no-op unless launched as a programmatic dependent
+  wait_for_prerequisite_grid();
+  allow_dependent_launch();
   constexpr int kLoads = 16;
   Acc a[4] = {Op::init(), Op::init(), Op::init(), Op::init()};
   int i = threadIdx.x;

@@ -137,19 +137,46 @@ inline bool launch_cluster_reduce(unsigned grid, const Ptrs<Body::kInputs>& in, 
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = grid;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   typename Op::Acc* no_partials = nullptr;
   if (cudaLaunchKernelEx(&cfg, reduce_vec_kernel<Op, Body, U, true>, no_partials, in, n, head,
                          body, out, partial_out) == cudaSuccess)
     return true;
   cudaGetLastError();
   return false;
+}
+
+// Every streaming kernel is launched as a programmatic dependent of the
+// kernel before it on the stream.  Each kernel first lets its own dependent
+// be scheduled (griddepcontrol.launch_dependents) and then waits for its
+// prerequisite grid to complete and flush (griddepcontrol.wait) before it
+// touches global memory, so stream order is kept; what is gained is that the
+// next kernel's first CTAs are already resident when this one ends.  After
+// a kernel that does not trigger (a library kernel, a copy) the launch simply
+// waits for it.  Where the attribute is refused, a plain launch is made.
+template <class Kern, class... Args>
+inline void launch_pdl(Kern kernel, unsigned grid, cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess) return;
+  cudaGetLastError();
+  kernel<<<grid, kThreads, 0, stream>>>(args...);
 }
 
 inline unsigned clamp_grid(int64_t g, int64_t cap) {
@@ -171,10 +198,10 @@ inline int launch_map(float* out, const Ptrs<Body::kInputs>& in, int64_t n, cons
     const int64_t tiles = ceil_div(nvec, (int64_t)kThreads * U);
     if (tiles > kMaxGrid) return LOOM_STATUS_INVALID_ARGUMENT;  // > 2^40 elements: no such GPU
     const unsigned grid = clamp_grid(tiles, kMaxGrid);
-    map_vec_kernel<Body, U><<<grid, kThreads, 0, stream>>>(out, in, n, head, body);
+    launch_pdl(map_vec_kernel<Body, U>, grid, stream, out, in, n, head, body);
   } else {
     const unsigned grid = clamp_grid(ceil_div(n, (int64_t)kThreads * kScalarUnroll), kMaxGrid);
-    map_scalar_kernel<Body><<<grid, kThreads, 0, stream>>>(out, in, n, body);
+    launch_pdl(map_scalar_kernel<Body>, grid, stream, out, in, n, body);
   }
   return launch_status();
 }
@@ -197,8 +224,8 @@ inline int launch_reduce(const Ptrs<Body::kInputs>& in, int64_t n, const Body& b
     if (grid > 1 && grid <= (unsigned)kMaxClusterCtas &&
         launch_cluster_reduce<Op, Body, U>(grid, in, n, head, body, out, partial_out, stream))
       return LOOM_STATUS_OK;
-    reduce_vec_kernel<Op, Body, U><<<grid, kThreads, 0, stream>>>(partials, in, n, head, body,
-                                                                   out, partial_out);
+    launch_pdl(reduce_vec_kernel<Op, Body, U>, grid, stream, partials, in, n, head, body, out,
+               partial_out);
   } else {
     grid = clamp_grid(ceil_div(n, (int64_t)kThreads * kScalarUnroll), max_partials);
     reduce_scalar_kernel<Op, Body><<<grid, kThreads, 0, stream>>>(partials, in, n, body, out,
