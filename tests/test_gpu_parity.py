@@ -193,3 +193,25 @@ def test_bound_call_matches_plain_call(suite_pkg, entry):
         call()
     torch.cuda.synchronize()
     assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("entry", SUMS + ["max_value"])
+def test_grid_sizes_around_the_cluster_limit(suite_pkg, oracle, entry):
+    # A reduction over up to 8 tiles is one cluster launch (DSMEM fold), above
+    # that a reduction kernel plus the finalize: sizes around 1, 2, 7, 8 and 9
+    # tiles (4096 elements per tile for one input, 2048 for two or three),
+    # aligned and with a 3-element head.
+    tile = 4096 if entry in ("l2_norm_sq", "max_value") else 2048
+    for g in (1, 2, 7, 8, 9):
+        for d in (-1, 0, 1):
+            n = g * tile + d
+            for offset in (0, 3):
+                inp = workloads.entry_inputs(entry, n, seed_offset=g * 10 + d)
+                ref = oracle.run(entry, inp)
+                dev = {k: (to_device(v, offset) if isinstance(v, np.ndarray) else v)
+                       for k, v in inp.items()}
+                got = float(suite_pkg[entry](**dev).cpu()[0])
+                if entry == "max_value":
+                    assert got == float(np.float32(ref)), (n, offset)
+                else:
+                    check_sum(entry, got, ref, inp, n)
