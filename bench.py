@@ -242,12 +242,19 @@ def make_inputs(n: int, rank: int):
     return data
 
 
-def launches_per_call(entry: str, world: int) -> int:
+def launches_per_call(entry: str, world: int, n: int) -> int:
+    """Kernels one call launches on n elements per GPU: one for a map; for a
+    reduction one when its grid is a single CTA or one cluster (at most 8
+    tiles of 256 threads x 4 float4 for one input, x 2 float4 for more),
+    else the reduction kernel and its finalize; plus the rank fold for sums
+    across GPUs."""
     if entry in MAP_ENTRIES:
         return 1
+    per_tile = 256 * 4 * (4 if len(TENSORS[entry]) == 1 else 2)
+    local = 1 if -(-n // per_tile) <= 8 else 2
     if world == 1:
-        return 2
-    return 3 if entry != "max_value" else 2  # + rank fold kernel for sums
+        return local
+    return local + (1 if entry != "max_value" else 0)
 
 
 def run_ours(args) -> None:
@@ -400,7 +407,7 @@ def run_ours(args) -> None:
                 "reasons": sorted({r for c in all_clocks for r in c["reasons"]}),
                 "per_rank_sm_mhz": [c["sm_mhz"] for c in all_clocks],
             },
-            "gpu_launches": args.steps * sum(launches_per_call(e, world) for e in ENTRIES),
+            "gpu_launches": args.steps * sum(launches_per_call(e, world, n) for e in ENTRIES),
             "e2e": e2e,
         }
         if ref_kernels is not None:
