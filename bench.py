@@ -694,6 +694,28 @@ def _median_us(call, reps: int, flush, stream) -> float:
     return statistics.median(times)
 
 
+def _median_wall_us(call, reps: int, flush) -> float:
+    """Median host wall time of `call` in us, the way the reference harness
+    times a kernel (experiments/source/harness/run.py:1154-1166): device
+    synchronise, perf_counter, the call, device synchronise, perf_counter;
+    with the same L2 flush as _median_us before each call."""
+    import torch
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        if flush is not None:
+            flush[0].fill_(1.0)
+            flush[1].sum()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        call()
+        torch.cuda.synchronize()
+        times.append((time.perf_counter() - t0) * 1e6)
+    return statistics.median(times)
+
+
 def _reference_calls(lib, entry, n, out, kw):
     """Bound reference-style calls of both profiles, with their workspaces."""
     import torch
@@ -716,10 +738,12 @@ def _timed_row(row, entry, nbytes, product_call, ref_calls, reps, flush, stream,
     row[entry + "_us"] = round(us, 2)
     row[entry + "_gbs"] = round(nbytes / (us * 1e-6) / 1e9, 1)
     row[entry + "_frac"] = round(nbytes / (us * 1e-6) / 1e9 / peak, 4)
+    row[entry + "_wall_us"] = round(_median_wall_us(product_call, reps, flush), 2)
     for profile, (call, _) in ref_calls.items():
         r_us = _median_us(call, reps, flush, stream)
         row[f"{entry}_ref_{profile}_us"] = round(r_us, 2)
         row[f"{entry}_ref_{profile}_gbs"] = round(nbytes / (r_us * 1e-6) / 1e9, 1)
+        row[f"{entry}_ref_{profile}_wall_us"] = round(_median_wall_us(call, reps, flush), 2)
 
 
 def run_pipeline_sweep(args) -> None:
