@@ -125,7 +125,10 @@ inline int launch_finalize(const typename Op::Acc* partials, int count, float* o
 
 // A grid of 2..kMaxClusterCtas CTAs launched as one thread-block cluster:
 // the CTAs fold their values through distributed shared memory, so the
-// reduction needs no finalize launch.  Returns false (with the error
+// reduction needs no finalize launch.  It is launched without the
+// programmatic-serialization attribute (its griddepcontrol.wait is then a
+// no-op): with both attributes the small-N call measured a full finalize
+// launch slower on B200.  Returns false (with the error
 // cleared) where the cluster launch is refused; the caller then takes the
 // two-launch path.
 template <class Op, class Body, int U>
@@ -137,15 +140,13 @@ inline bool launch_cluster_reduce(unsigned grid, const Ptrs<Body::kInputs>& in, 
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = grid;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
   typename Op::Acc* no_partials = nullptr;
   if (cudaLaunchKernelEx(&cfg, reduce_vec_kernel<Op, Body, U, true>, no_partials, in, n, head,
                          body, out, partial_out) == cudaSuccess)
