@@ -1,0 +1,141 @@
+"""`python -m loom_b200 package`, exercised the way the reference's own
+package tests exercise `loomc package` (test/python/test_package.py:29-165):
+a project with a `kernels` module holding saxpy, relu and dot is packaged as
+a shared library and, with module/entry filters and an optimisation flag, as
+a static archive; the artefact layout and manifest fields are checked on CPU,
+and on a GPU the shared library is bound with plain ctypes and compared with
+torch at the reference tests' tolerance (rtol 1e-4, atol 1e-5)."""
+
+import ctypes
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+KERNELS = '''import loom
+
+
+@loom.entry
+def saxpy(a: float, x: loom.Tensor1, y: loom.Tensor1) -> loom.Tensor1:
+    return loom.Tensor1.map2(lambda xi, yi: a * xi + yi, x, y)
+
+
+@loom.entry
+def relu(x: loom.Tensor1) -> loom.Tensor1:
+    return loom.Tensor1.map(lambda xi: xi if xi > 0.0 else 0.0, x)
+
+
+@loom.entry
+def dot(x: loom.Tensor1, y: loom.Tensor1) -> float:
+    products = loom.Tensor1.map2(lambda xi, yi: xi * yi, x, y)
+    return loom.Tensor1.reduce_sum(products)
+'''
+
+
+def _project(tmp_path):
+    proj = tmp_path / "package_project"
+    proj.mkdir()
+    (proj / "kernels.py").write_text(KERNELS)
+    return proj
+
+
+def _package(*args):
+    return subprocess.run([sys.executable, "-m", "loom_b200", "package", *args], cwd=ROOT,
+                          capture_output=True, text=True)
+
+
+@pytest.fixture(scope="module")
+def shared_package(tmp_path_factory):
+    tmp = tmp_path_factory.mktemp("pkg_shared")
+    proj = _project(tmp)
+    out = tmp / "out"
+    result = _package("--project", str(proj), "--out", str(out))
+    assert result.returncode == 0, result.stderr
+    return out
+
+
+def test_package_shared_layout(shared_package):
+    out = shared_package
+    for rel in ("libpackage_project.so", "include/loom/package_project.h",
+                "src-gen/package_project.cu", "manifest.json", "report.md",
+                "entries/loom_kernels_saxpy/tensor_ir.json",
+                "entries/loom_kernels_dot/kernel_plan.json",
+                "entries/loom_kernels_dot/cuda_plan.json",
+                "entries/loom_kernels_dot/backend_analysis.json"):
+        assert (out / rel).exists(), rel
+    manifest = json.loads((out / "manifest.json").read_text())
+    assert manifest["target_backend"] == "cuda"
+    assert manifest["artifact_kind"] == "shared"
+    assert sorted(e["entry_name"] for e in manifest["entries"]) == ["dot", "relu", "saxpy"]
+    by_name = {e["entry_name"]: e for e in manifest["entries"]}
+    assert by_name["saxpy"]["no_workspace_symbol"] == "loom_kernels_saxpy_noworkspace"
+    assert by_name["dot"]["workspace_symbol"] == "loom_kernels_dot_workspace_size"
+    assert [p["kind"] for p in by_name["saxpy"]["params"]] == [
+        "scalar-f32", "tensor1-f32", "tensor1-f32"]
+    assert by_name["dot"]["result_kind"] == "scalar"
+
+
+def test_package_static_with_filters(tmp_path):
+    proj = _project(tmp_path)
+    out = tmp_path / "out"
+    result = _package("--project", str(proj), "--out", str(out), "--kind", "static",
+                      "--module", "kernels", "--entry", "relu",
+                      "--enable-opt", "elementwise-plan-specialize")
+    assert result.returncode == 0, result.stderr
+    manifest = json.loads((out / "manifest.json").read_text())
+    assert (out / "libpackage_project.a").exists()
+    assert manifest["target_backend"] == "cuda"
+    assert manifest["artifact_kind"] == "static"
+    assert manifest["optimizations"]["enabled"] == ["elementwise-plan-specialize"]
+    assert len(manifest["entries"]) == 1
+    assert manifest["entries"][0]["entry_name"] == "relu"
+    assert manifest["entries"][0]["symbol_name"] == "loom_kernels_relu"
+
+
+def test_package_rejects_another_arch(tmp_path):
+    proj = _project(tmp_path)
+    result = _package("--project", str(proj), "--out", str(tmp_path / "o"), "--cuda-arch",
+                      "sm_90a")
+    assert result.returncode != 0 and "sm_100a" in result.stderr
+
+
+@pytest.mark.gpu
+def test_package_shared_library_runtime(shared_package):
+    import torch
+
+    def ptr(t):
+        return ctypes.c_void_p(t.data_ptr())
+
+    lib = ctypes.CDLL(str(shared_package / "libpackage_project.so"))
+    saxpy_ws = lib.loom_kernels_saxpy_workspace_size
+    saxpy_ws.argtypes = [ctypes.c_longlong]
+    saxpy_ws.restype = ctypes.c_size_t
+    assert saxpy_ws(4096) == 0
+    saxpy = lib.loom_kernels_saxpy
+    saxpy.argtypes = [ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong,
+                      ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t]
+    saxpy.restype = ctypes.c_int
+    n, a = 4096, 2.5
+    x = torch.randn(n, device="cuda")
+    y = torch.randn(n, device="cuda")
+    out = torch.empty_like(x)
+    assert saxpy(ctypes.c_float(a), ptr(x), ptr(y), n, ptr(out), None, 0) == 0
+    torch.testing.assert_close(out, a * x + y, rtol=1e-4, atol=1e-5)
+
+    dot_ws = lib.loom_kernels_dot_workspace_size
+    dot_ws.argtypes = [ctypes.c_longlong]
+    dot_ws.restype = ctypes.c_size_t
+    size = dot_ws(n)
+    assert size > 0
+    dot = lib.loom_kernels_dot
+    dot.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p,
+                    ctypes.c_void_p, ctypes.c_size_t]
+    dot.restype = ctypes.c_int
+    s = torch.empty(1, device="cuda")
+    ws = torch.empty(size, device="cuda", dtype=torch.uint8)
+    assert dot(ptr(x), ptr(y), n, ptr(s), ptr(ws), size) == 0
+    torch.testing.assert_close(s[0], torch.sum(x * y), rtol=1e-4, atol=1e-5)
