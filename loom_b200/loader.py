@@ -86,14 +86,18 @@ class Entry:
     def workspace_size(self, n: int) -> int:
         return int(self.ws_fn(int(n)))
 
-    def workspace(self, n: int, device=None, dist: bool = False):
-        """Cached device workspace for n elements (None when not needed)."""
+    def workspace(self, n: int, device=None, dist: bool = False, stream=None):
+        """Cached device workspace for n elements (None when not needed).
+        One workspace per (device, stream, size): calls on one stream are
+        ordered by that stream, and calls on different streams, which may
+        run at the same time, never share one."""
         torch = _torch()
         size = int(self.dist_ws_fn(n)) if dist else self.workspace_size(n)
         if size <= 0:
             return None
         device = torch.device(device if device is not None else "cuda")
-        key = (str(device), size)
+        handle = int(getattr(stream, "cuda_stream", stream) or 0)
+        key = (str(device), handle, size)
         ws = self._ws.get(key)
         if ws is None:
             ws = torch.empty(size, dtype=torch.uint8, device=device)
@@ -137,7 +141,7 @@ class Entry:
         if out is None:
             out = self.new_output(n, device)
         args = self._args(inputs, n)
-        ws = self.workspace(n, device)
+        ws = self.workspace(n, device, stream=stream)
         wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
         wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
         tail = [ctypes.c_int64(n), ctypes.c_void_p(out.data_ptr()), wsp, wss]
@@ -161,7 +165,7 @@ class Entry:
         if out is None:
             out = self.new_output(n, device)
         args = self._args(inputs, n)
-        ws = self.workspace(n, device)
+        ws = self.workspace(n, device, stream=stream)
         wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
         wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
         handle = getattr(stream, "cuda_stream", stream) if stream is not None else 0
@@ -187,7 +191,7 @@ class Entry:
         if out is None:
             out = self.new_output(n, device)
         args = self._args(inputs, n)
-        ws = self.workspace(n, device, dist=True)
+        ws = self.workspace(n, device, dist=True, stream=stream)
         wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
         wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
         handle = getattr(stream, "cuda_stream", stream) if stream is not None else None
