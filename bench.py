@@ -716,6 +716,34 @@ def _median_wall_us(call, reps: int, flush) -> float:
     return statistics.median(times)
 
 
+def _graph_us(entry_obj, kw, out, calls: int = 20, replays: int = 20) -> float:
+    """Per-call device time of `calls` back-to-back calls captured in one CUDA
+    graph on a side stream and replayed `replays` times (no flush: the
+    launch-bound regime this is meant for)."""
+    import torch
+    side = torch.cuda.Stream()
+    call, _ = entry_obj.bind(out=out, stream=side, **kw)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        for _ in range(calls):
+            call()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    a.record(cur)
+    for _ in range(replays):
+        graph.replay()
+    b.record(cur)
+    b.synchronize()
+    us = a.elapsed_time(b) * 1e3 / (calls * replays)
+    del graph
+    return us
+
+
 def _reference_calls(lib, entry, n, out, kw):
     """Bound reference-style calls of both profiles, with their workspaces."""
     import torch
@@ -753,8 +781,11 @@ def run_pipeline_sweep(args) -> None:
     reference-style kernels of both profiles on the same inputs.  A 512 MiB
     buffer is rewritten (then another read) before every timed call, so
     that no input is served from L2 and the kernels' cache hints cannot
-    favour one side through lines left over from the previous call.  Every call is bound once, so
-    the per-call host work is the same for both.  Prints one JSON line."""
+    favour one side through lines left over from the previous call.  Every
+    call is bound once, so the per-call host work is the same for both.  Up
+    to 2^26 the product is also timed as 20 back-to-back calls replayed from
+    one CUDA graph (`*_graph_us`, per call, no flush).  Prints one JSON
+    line."""
     import torch
     from baseline.reference_style import ReferenceStyle
     from loom_b200.build import load_suite
@@ -788,6 +819,9 @@ def run_pipeline_sweep(args) -> None:
         call, _ = pkg["pipeline_sum"].bind(out=s, stream=stream, **ks)
         _timed_row(row, "pipeline_sum", 12 * n, call, refs, reps, flush, stream, peak)
         del refs
+        if n <= (1 << 26):
+            row["affine_relu_graph_us"] = round(_graph_us(pkg["affine_relu"], kz, z), 2)
+            row["pipeline_sum_graph_us"] = round(_graph_us(pkg["pipeline_sum"], ks, s), 2)
         points.append(row)
         del x, y, w, z
         torch.cuda.empty_cache()
