@@ -363,7 +363,10 @@ def run_ours(args) -> None:
                           "frac": round(gbs / peak, 4), "bytes_per_elem": bytes_per_elem(e)}
         dom = max(ENTRIES, key=lambda e: kernels[e]["us_per_call"])
         dom_bytes = bytes_per_elem(dom) * n
-        dom_traffic = traffic.get(dom, {}).get("dram_bytes_per_launch_at_2^28")
+        # ncu's DRAM bytes of one launch at 2^26, scaled to this N: the reads
+        # are the algorithmic bytes exactly, so traffic grows in proportion
+        measured = traffic.get(dom, {}).get("dram_bytes_per_launch_at_2^26")
+        dom_traffic = int(measured * n / (1 << 26)) if measured else None
         line = {
             "metric": METRIC,
             "value": round(value, 1),
