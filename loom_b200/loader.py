@@ -125,6 +125,27 @@ class Entry:
     def _n(self, inputs: Dict[str, object]) -> int:
         return int(inputs[self.tensor_params[0]].numel())
 
+    def _device(self, inputs: Dict[str, object]):
+        """The one CUDA device that holds every tensor input."""
+        devs = {inputs[t].device for t in self.tensor_params if hasattr(inputs[t], "device")}
+        if len(devs) != 1:
+            raise ValueError(f"{self.name}: tensor inputs must be on one CUDA device, got "
+                             f"{sorted(str(d) for d in devs)}")
+        return devs.pop()
+
+    def _check_out(self, out, n: int, device) -> None:
+        """The output must hold the whole result on the inputs' device: the
+        kernels write n floats (1 for a scalar result) through it."""
+        torch = _torch()
+        need = n if self.result_kind == "tensor" else 1
+        if not (isinstance(out, torch.Tensor) and out.is_cuda and out.dtype == torch.float32
+                and out.is_contiguous()):
+            raise TypeError(f"{self.name}: out must be a contiguous float32 CUDA tensor")
+        if out.device != device:
+            raise ValueError(f"{self.name}: out is on {out.device}, inputs on {device}")
+        if out.numel() < need:
+            raise ValueError(f"{self.name}: out has {out.numel()} elements, needs {need}")
+
     def new_output(self, n: int, device):
         torch = _torch()
         if self.result_kind == "tensor":
@@ -136,20 +157,23 @@ class Entry:
         """Run on device tensors; returns the output tensor (n floats, or 1
         float for a scalar result).  With `stream` (a torch.cuda.Stream or a
         raw handle) the call is asynchronous on that stream."""
+        torch = _torch()
         n = self._n(inputs)
-        device = inputs[self.tensor_params[0]].device
+        args = self._args(inputs, n)
+        device = self._device(inputs)
         if out is None:
             out = self.new_output(n, device)
-        args = self._args(inputs, n)
-        ws = self.workspace(n, device, stream=stream)
-        wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
-        wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
-        tail = [ctypes.c_int64(n), ctypes.c_void_p(out.data_ptr()), wsp, wss]
-        if stream is None:
-            status = self.fn(*args, *tail)
-        else:
-            handle = getattr(stream, "cuda_stream", stream)
-            status = self.stream_fn(*args, *tail, ctypes.c_void_p(handle))
+        self._check_out(out, n, device)
+        with torch.cuda.device(device):
+            ws = self.workspace(n, device, stream=stream)
+            wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
+            wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
+            tail = [ctypes.c_int64(n), ctypes.c_void_p(out.data_ptr()), wsp, wss]
+            if stream is None:
+                status = self.fn(*args, *tail)
+            else:
+                handle = getattr(stream, "cuda_stream", stream)
+                status = self.stream_fn(*args, *tail, ctypes.c_void_p(handle))
         if status != 0:
             raise LoomError(self.symbol, status)
         return out
@@ -161,10 +185,14 @@ class Entry:
         For launch loops where the per-call Python work would show, and for
         stream capture.  The tensors must stay alive while `call` is used."""
         n = self._n(inputs)
-        device = inputs[self.tensor_params[0]].device
+        args = self._args(inputs, n)
+        device = self._device(inputs)
+        if device.index != _torch().cuda.current_device():
+            raise ValueError(f"{self.name}: bind with the inputs' device ({device}) current; "
+                             "the bound call launches on the current device")
         if out is None:
             out = self.new_output(n, device)
-        args = self._args(inputs, n)
+        self._check_out(out, n, device)
         ws = self.workspace(n, device, stream=stream)
         wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
         wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
@@ -187,10 +215,11 @@ class Entry:
         if self.dist_fn is None:
             raise RuntimeError(f"{self.package.name} was built without multi-GPU entries")
         n = self._n(inputs)
-        device = inputs[self.tensor_params[0]].device
+        args = self._args(inputs, n)
+        device = self._device(inputs)
         if out is None:
             out = self.new_output(n, device)
-        args = self._args(inputs, n)
+        self._check_out(out, n, device)
         ws = self.workspace(n, device, dist=True, stream=stream)
         wsp = ctypes.c_void_p(ws.data_ptr()) if ws is not None else None
         wss = ctypes.c_size_t(ws.numel() if ws is not None else 0)
@@ -309,6 +338,8 @@ class Entry:
         if outs is None:
             outs = [self.new_output(ns[d], shards[d][self.tensor_params[0]].device)
                     for d in range(nd)]
+        for d in range(nd):
+            self._check_out(outs[d], ns[d], self._device(shards[d]))
         keep = []
         args = [ctypes.c_int(nd), (ctypes.c_void_p * nd)(*[c.handle for c in comms])]
         for p in self.params:

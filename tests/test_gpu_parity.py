@@ -215,3 +215,23 @@ def test_grid_sizes_around_the_cluster_limit(suite_pkg, oracle, entry):
                     assert got == float(np.float32(ref)), (n, offset)
                 else:
                     check_sum(entry, got, ref, inp, n)
+
+
+def test_loader_rejects_bad_outputs_and_mixed_devices(suite_pkg):
+    # the loader checks what the C ABI cannot: the output's size, type and
+    # device, before anything is launched
+    x = torch.zeros(1000, device="cuda")
+    y = torch.zeros(1000, device="cuda")
+    with pytest.raises(ValueError):
+        suite_pkg["saxpy"](out=torch.empty(999, device="cuda"), a=1.0, x=x, y=y)
+    with pytest.raises(TypeError):
+        suite_pkg["saxpy"](out=torch.empty(1000, device="cuda", dtype=torch.float64),
+                           a=1.0, x=x, y=y)
+    with pytest.raises(TypeError):
+        suite_pkg["dot"](out=torch.empty(1), x=x, y=y)         # a host tensor
+    with pytest.raises(ValueError):
+        suite_pkg["dot"](x=x, y=torch.zeros(999, device="cuda"))
+    assert suite_pkg["dot"](out=torch.empty(4, device="cuda"), x=x, y=y)[0].item() == 0.0
+    if torch.cuda.device_count() > 1:
+        with pytest.raises(ValueError):
+            suite_pkg["dot"](x=x, y=torch.zeros(1000, device="cuda:1"))
