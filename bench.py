@@ -242,18 +242,21 @@ def make_inputs(n: int, rank: int):
     return data
 
 
-def launches_per_call(entry: str, world: int, n: int) -> int:
-    """Kernels one call launches on n elements per GPU: one for a map; for a
-    reduction one when its grid is a single CTA or one cluster (at most 8
-    tiles of 256 threads x 4 float4 for one input, x 2 float4 for more),
-    else the reduction kernel and its finalize; plus the rank fold for sums
-    across GPUs."""
+def launches_per_call(entry: str, world: int, n: int, peer: bool = True) -> int:
+    """Kernels of this library one call launches on n elements per GPU: one
+    for a map; for a reduction one when its grid is a single CTA or one
+    cluster (at most 8 tiles of 256 threads x 4 float4 for one input, x 2
+    float4 for more), else the reduction kernel and its finalize; across
+    GPUs plus the exchange kernel (peer memory) or, with NCCL, the rank fold
+    for sums (NCCL's own kernels are not counted)."""
     if entry in MAP_ENTRIES:
         return 1
     per_tile = 256 * 4 * (4 if len(TENSORS[entry]) == 1 else 2)
     local = 1 if -(-n // per_tile) <= 8 else 2
     if world == 1:
         return local
+    if peer:
+        return local + 1
     return local + (1 if entry != "max_value" else 0)
 
 
@@ -270,6 +273,8 @@ def run_ours(args) -> None:
     data = make_inputs(n, rank)
     outs = {e: torch.empty(n if e in MAP_ENTRIES else 1, device="cuda") for e in ENTRIES}
     comm = pkg.comm_from_process_group() if world > 1 else None
+    if comm is not None and args.exchange == "nccl":
+        comm.set_peer_exchange(False)
     stream = torch.cuda.current_stream()
 
     # Pre-bind every call (no Python tensor work inside the timed loop).
@@ -390,7 +395,10 @@ def run_ours(args) -> None:
                 "entries": ENTRIES,
                 "l2": "no flush: every input is 1 GiB per GPU (> 126 MB L2)",
                 "parallelism": f"shard{world} (maps: no communication; reductions: one "
-                               "scalar NCCL collective)",
+                               "scalar exchange per call)",
+                "exchange": (None if comm is None else
+                             ("peer memory (NVLink P2P stores)" if comm.peer_exchange
+                              else "NCCL all-gather / all-reduce")),
             },
             "kernels": kernels,
             "roofline": {
@@ -410,7 +418,9 @@ def run_ours(args) -> None:
                 "reasons": sorted({r for c in all_clocks for r in c["reasons"]}),
                 "per_rank_sm_mhz": [c["sm_mhz"] for c in all_clocks],
             },
-            "gpu_launches": args.steps * sum(launches_per_call(e, world, n) for e in ENTRIES),
+            "gpu_launches": args.steps * sum(
+                launches_per_call(e, world, n, comm is not None and comm.peer_exchange)
+                for e in ENTRIES),
             "e2e": e2e,
         }
         if ref_kernels is not None:
@@ -421,6 +431,7 @@ def run_ours(args) -> None:
             line["cpu_baseline"] = cpu_baseline(args.cpu_log2, args.cpu_seconds)
         emit(line)
     if comm is not None:
+        comm.check()
         comm.destroy()
     if world > 1:
         import torch.distributed as dist
@@ -891,6 +902,9 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                    help="scalar exchange of the reductions across GPUs: peer memory "
+                         "(where every GPU reaches the others) or NCCL")
     ap.add_argument("--ref-kernel-steps", type=int, default=30,
                     help="steps of the reference-style GPU kernels (1 GPU; 0 skips them)")
     ap.add_argument("--cpu-log2", type=int, default=24)

@@ -116,6 +116,10 @@ def comm_prototypes(package: str) -> List[str]:
         f"int {p}_init_rank(void** comm_out, int nranks, int rank, const void* id, size_t id_size);",
         f"int {p}_init_all(void** comms_out, int ndev, const int* devices);",
         f"int {p}_destroy(void* comm);",
+        f"int {p}_set_peer_exchange(void* comm, int enable);",
+        f"int {p}_set_timeout_ms(void* comm, int64_t ms);",
+        f"int {p}_peer_exchange(void* comm);",
+        f"int {p}_check(void* comm);",
     ]
 
 
@@ -150,8 +154,11 @@ def render_header(package: str, plans: List[EntryPlan], multi_gpu: bool = True,
             lines.append(noalloc_prototype(plan))
     if multi_gpu:
         lines.append("")
-        lines.append("/* NCCL communicators for the _dist and _multi entries (additive; the "
-                     "reference has no multi-GPU path). */")
+        lines.append("/* Communicators for the _dist and _multi entries (additive; the reference has "
+                     "no multi-GPU path): NCCL, plus a peer-memory scalar exchange where every GPU "
+                     "reaches the others'. _set_peer_exchange switches paths (every rank alike); "
+                     "an exchange waits at most _set_timeout_ms (30 s by default) for the other "
+                     "ranks; _check reports one that gave up. */")
         lines += comm_prototypes(package)
     lines += ["", "#ifdef __cplusplus", "}", "#endif", ""]
     return "\n".join(lines)
@@ -308,8 +315,9 @@ def _render_dist(plan: EntryPlan, async_return: bool) -> List[str]:
 
 def _render_multi(plan: EntryPlan, async_return: bool) -> List[str]:
     """One process, ``ndev`` GPUs: local shards on every device, then (for a
-    reduction) one grouped NCCL collective across the communicators, then the
-    rank fold on every device."""
+    reduction) the scalar exchange: through peer memory where the
+    communicators set it up, else one grouped NCCL collective and the rank
+    fold on every device."""
     sym = plan.symbol
     decls = ["int ndev", "void* const* comms"] + _multi_param_decls(plan) + [
         "const int64_t* shard_n", "float* const* out", "void* const* workspace",
@@ -356,22 +364,9 @@ def _render_multi(plan: EntryPlan, async_return: bool) -> List[str]:
                  "workspace[loom_d], nullptr);")
         L.append("    if (loom_status != LOOM_STATUS_OK) return loom_status;")
         L.append("  }")
-        L.append("  if (loomb::nccl_group_start() != 0) return LOOM_STATUS_COMM_ERROR;")
-        L.append("  int loom_group_status = LOOM_STATUS_OK;")
-        L.append("  for (int loom_d = 0; loom_d < ndev && loom_group_status == LOOM_STATUS_OK; ++loom_d) {")
-        L.append("    loomb::Comm* loom_c = static_cast<loomb::Comm*>(comms[loom_d]);")
-        L.append(f"    loom_group_status = loomb::dist_collective<{op}>(workspace[loom_d], shard_n[loom_d], out[loom_d], "
-                 "loom_c, nullptr);")
-        L.append("  }")
-        L.append("  if (loomb::nccl_group_end() != 0) return LOOM_STATUS_COMM_ERROR;")
-        L.append("  if (loom_group_status != LOOM_STATUS_OK) return loom_group_status;")
-        L.append("  for (int loom_d = 0; loom_d < ndev; ++loom_d) {")
-        L.append("    loomb::Comm* loom_c = static_cast<loomb::Comm*>(comms[loom_d]);")
-        L.append("    if (cudaSetDevice(loom_c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
-        L.append(f"    const int loom_status = loomb::dist_finish<{op}>(workspace[loom_d], shard_n[loom_d], out[loom_d], "
-                 "loom_c, nullptr);")
-        L.append("    if (loom_status != LOOM_STATUS_OK) return loom_status;")
-        L.append("  }")
+        L.append(f"  const int loom_exchange = loomb::multi_exchange<{op}>(ndev, comms, workspace, "
+                 "shard_n, out);")
+        L.append("  if (loom_exchange != LOOM_STATUS_OK) return loom_exchange;")
         L.append("  if (host_result != nullptr) {")
         L.append("    loomb::Comm* loom_c0 = static_cast<loomb::Comm*>(comms[0]);")
         L.append("    if (cudaSetDevice(loom_c0->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
@@ -404,6 +399,14 @@ def render_comm_api(package: str) -> str:
         "  return loomb::comm_init_all(comms_out, ndev, devices);",
         "}",
         f'extern "C" int {p}_destroy(void* comm) {{ return loomb::comm_destroy(comm); }}',
+        f'extern "C" int {p}_set_peer_exchange(void* comm, int enable) {{',
+        "  return loomb::comm_set_peer_exchange(comm, enable);",
+        "}",
+        f'extern "C" int {p}_set_timeout_ms(void* comm, int64_t ms) {{',
+        "  return loomb::comm_set_timeout_ms(comm, ms);",
+        "}",
+        f'extern "C" int {p}_peer_exchange(void* comm) {{ return loomb::comm_peer_exchange(comm); }}',
+        f'extern "C" int {p}_check(void* comm) {{ return loomb::comm_check(comm); }}',
         "",
     ])
 

@@ -12,6 +12,14 @@
 //    from run to run;
 //  * max: fp32 ncclMax all-reduce of the per-rank maxima (exact in any order).
 //
+// Where every pair of GPUs can reach each other's memory (NVLink / NVSwitch),
+// the scalar exchange does not go through NCCL at all: each rank's exchange
+// kernel stores its value straight into every peer's exchange buffer (P2P
+// stores over NVLink), then reads the nranks values from its own buffer and
+// folds them in rank order -- the same values in the same order as the NCCL
+// path, so the same bits.  That replaces an NCCL collective and a fold kernel
+// by one single-thread kernel (see peer_exchange_kernel).
+//
 // Communicators are explicit handles created by the caller (one process per
 // GPU via comm_init_rank, or one process for several GPUs via comm_init_all)
 // and destroyed with comm_destroy; the library keeps no global state.
@@ -32,11 +40,40 @@
 
 namespace loomb {
 
+// Every rank's exchange buffer, as addressed from this rank's device.
+struct PeerTable {
+  unsigned char* buf[kMaxRanks];
+};
+
+// Layout of an exchange buffer (kExchangeBytes, zeroed at creation):
+//   +0   u64  exchanges this rank has made (its epoch counter)
+//   +8   u32  status: 0 ok, 1 a wait for a peer ran out
+//   +64  ExchangeSlot[2][kMaxRanks]: the value each rank sent for the
+//        exchanges of even / odd epoch.  Two sets suffice: a rank can be at
+//        most one exchange ahead of any other, since it cannot finish an
+//        exchange before every rank has sent to it.
+struct ExchangeSlot {
+  unsigned long long bits;
+  unsigned long long epoch;
+};
+constexpr size_t kExchangeSlotsOffset = 64;
+constexpr size_t kExchangeBytes = 4096;
+static_assert(kExchangeSlotsOffset + 2 * kMaxRanks * sizeof(ExchangeSlot) + 64 +
+                      kMaxRanks * sizeof(cudaIpcMemHandle_t) + 64 <=
+                  kExchangeBytes,
+              "exchange buffer too small for the slots and the setup scratch");
+
 struct Comm {
   ncclComm_t nccl = nullptr;
   int nranks = 0;
   int rank = 0;
   int device = 0;
+  unsigned char* xbuf = nullptr;     // this rank's exchange buffer (device memory)
+  PeerTable peers = {};              // every rank's buffer, from this device
+  bool ipc_opened[kMaxRanks] = {};   // peers mapped with cudaIpcOpenMemHandle
+  bool peer_capable = false;         // the buffers are set up on every rank
+  bool peer_exchange = false;        // exchange through peer memory (else NCCL)
+  unsigned long long timeout_ns = 30000000000ull;  // a peer exchange's wait limit
 };
 
 // Restores the caller's current device when it goes out of scope.
@@ -47,6 +84,121 @@ struct DeviceGuard {
     if (device >= 0) cudaSetDevice(device);
   }
 };
+
+inline void release_exchange(Comm* c) {
+  for (int r = 0; r < kMaxRanks; ++r) {
+    if (c->ipc_opened[r]) cudaIpcCloseMemHandle(c->peers.buf[r]);
+    c->ipc_opened[r] = false;
+    c->peers.buf[r] = nullptr;
+  }
+  if (c->xbuf != nullptr) cudaFree(c->xbuf);
+  c->xbuf = nullptr;
+  c->peer_capable = c->peer_exchange = false;
+}
+
+inline bool alloc_exchange(Comm* c) {
+  if (cudaMalloc(&c->xbuf, kExchangeBytes) != cudaSuccess) {
+    c->xbuf = nullptr;
+    cudaGetLastError();
+    return false;
+  }
+  return cudaMemset(c->xbuf, 0, kExchangeBytes) == cudaSuccess &&
+         cudaDeviceSynchronize() == cudaSuccess;
+}
+
+// One process per GPU: every rank exports its exchange buffer with a CUDA
+// IPC handle, the handles are all-gathered over the new communicator, and
+// every rank maps the others' buffers.  The ranks then agree (an NCCL min of
+// a success flag) so that either all of them use peer memory or none does.
+// A failure to map leaves every rank on the NCCL path.  The setup scratch
+// (nranks handles and the flag) sits behind the exchange area of the same
+// allocation; a rank that could not make even that allocation would leave
+// the others waiting in the collective, as a failure inside
+// ncclCommInitRank would.
+inline void setup_exchange_ipc(Comm* c) {
+  constexpr size_t kH = sizeof(cudaIpcMemHandle_t);
+  bool ok = alloc_exchange(c);
+  if (!ok) {
+    release_exchange(c);
+    return;
+  }
+  unsigned char* scratch = c->xbuf + kExchangeSlotsOffset + 2 * kMaxRanks * sizeof(ExchangeSlot);
+  scratch = reinterpret_cast<unsigned char*>(align_up((size_t)(uintptr_t)scratch, 64));
+  cudaIpcMemHandle_t own;
+  memset(&own, 0, sizeof(own));
+  ok = cudaIpcGetMemHandle(&own, c->xbuf) == cudaSuccess;
+  unsigned char host[kMaxRanks * kH];
+  cudaMemcpy(scratch + (size_t)c->rank * kH, &own, kH, cudaMemcpyHostToDevice);
+  const bool gathered =
+      ncclAllGather(scratch + (size_t)c->rank * kH, scratch, kH, ncclChar, c->nccl, nullptr) ==
+          ncclSuccess &&
+      cudaStreamSynchronize(nullptr) == cudaSuccess &&
+      cudaMemcpy(host, scratch, c->nranks * kH, cudaMemcpyDeviceToHost) == cudaSuccess;
+  ok = ok && gathered;
+  for (int r = 0; r < c->nranks && ok; ++r) {
+    if (r == c->rank) {
+      c->peers.buf[r] = c->xbuf;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, host + (size_t)r * kH, kH);
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      ok = false;
+      break;
+    }
+    c->peers.buf[r] = static_cast<unsigned char*>(p);
+    c->ipc_opened[r] = true;
+  }
+  int flag = ok ? 1 : 0;
+  int* dflag = reinterpret_cast<int*>(scratch + (size_t)c->nranks * kH);
+  const bool agreed =
+      cudaMemcpy(dflag, &flag, sizeof(int), cudaMemcpyHostToDevice) == cudaSuccess &&
+      ncclAllReduce(dflag, dflag, 1, ncclInt32, ncclMin, c->nccl, nullptr) == ncclSuccess &&
+      cudaStreamSynchronize(nullptr) == cudaSuccess &&
+      cudaMemcpy(&flag, dflag, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && flag == 1;
+  // the scratch is not part of the exchange area; clear it again
+  cudaMemset(scratch, 0, (size_t)c->nranks * kH + sizeof(int));
+  cudaDeviceSynchronize();
+  if (!agreed) {
+    release_exchange(c);
+    return;
+  }
+  c->peer_capable = c->peer_exchange = true;
+}
+
+// One process, several GPUs: direct peer access between every pair.
+inline void setup_exchange_local(Comm** cs, int ndev) {
+  bool ok = true;
+  for (int d = 0; d < ndev && ok; ++d) {
+    ok = cudaSetDevice(cs[d]->device) == cudaSuccess && alloc_exchange(cs[d]);
+  }
+  for (int i = 0; i < ndev && ok; ++i) {
+    for (int j = 0; j < ndev && ok; ++j) {
+      if (i == j) continue;
+      int can = 0;
+      if (cudaDeviceCanAccessPeer(&can, cs[i]->device, cs[j]->device) != cudaSuccess || !can) {
+        ok = false;
+        break;
+      }
+      cudaSetDevice(cs[i]->device);
+      const cudaError_t e = cudaDeviceEnablePeerAccess(cs[j]->device, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();
+      else if (e != cudaSuccess) ok = false;
+    }
+  }
+  for (int d = 0; d < ndev; ++d) {
+    cudaSetDevice(cs[d]->device);
+    if (!ok) {
+      cudaGetLastError();
+      release_exchange(cs[d]);
+      continue;
+    }
+    for (int r = 0; r < ndev; ++r) cs[d]->peers.buf[r] = cs[r]->xbuf;
+    cs[d]->peer_capable = cs[d]->peer_exchange = true;
+  }
+}
 
 inline int comm_id_size() { return (int)sizeof(ncclUniqueId); }
 
@@ -79,6 +231,7 @@ inline int comm_init_rank(void** comm_out, int nranks, int rank, const void* id,
   }
   c->nranks = nranks;
   c->rank = rank;
+  if (nranks > 1) setup_exchange_ipc(c);
   *comm_out = c;
   return LOOM_STATUS_OK;
 }
@@ -107,15 +260,62 @@ inline int comm_init_all(void** comms_out, int ndev, const int* devices) {
     c->device = devices[d];
     comms_out[d] = c;
   }
+  if (ndev > 1) {
+    DeviceGuard guard;
+    setup_exchange_local(reinterpret_cast<Comm**>(comms_out), ndev);
+  }
   return LOOM_STATUS_OK;
 }
 
 inline int comm_destroy(void* comm) {
   if (comm == nullptr) return LOOM_STATUS_OK;
   Comm* c = static_cast<Comm*>(comm);
+  {
+    DeviceGuard guard;
+    cudaSetDevice(c->device);
+    cudaDeviceSynchronize();
+    release_exchange(c);
+  }
   const ncclResult_t r = ncclCommDestroy(c->nccl);
   delete c;
   return r == ncclSuccess ? LOOM_STATUS_OK : LOOM_STATUS_COMM_ERROR;
+}
+
+// Choose the exchange path: 1 peer memory (only where it was set up), 0
+// NCCL.  Collective in effect: every rank must make the same choice before
+// its next reduction, or the ranks wait for values that never come (the
+// waits are bounded; see comm_check).
+inline int comm_set_peer_exchange(void* comm, int enable) {
+  if (comm == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;
+  Comm* c = static_cast<Comm*>(comm);
+  if (enable && !c->peer_capable) return LOOM_STATUS_INVALID_ARGUMENT;
+  c->peer_exchange = enable != 0;
+  return LOOM_STATUS_OK;
+}
+
+// The wait limit of this rank's peer exchanges, in milliseconds (> 0).
+inline int comm_set_timeout_ms(void* comm, int64_t ms) {
+  if (comm == nullptr || ms <= 0 || ms > 3600000) return LOOM_STATUS_INVALID_ARGUMENT;
+  static_cast<Comm*>(comm)->timeout_ns = (unsigned long long)ms * 1000000ull;
+  return LOOM_STATUS_OK;
+}
+
+inline int comm_peer_exchange(void* comm) {
+  return comm != nullptr && static_cast<Comm*>(comm)->peer_exchange ? 1 : 0;
+}
+
+// Waits for this rank's device and reports whether any peer exchange gave up
+// waiting for another rank (COMM_ERROR; the affected results were NaN).
+inline int comm_check(void* comm) {
+  if (comm == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;
+  Comm* c = static_cast<Comm*>(comm);
+  if (c->xbuf == nullptr) return LOOM_STATUS_OK;
+  DeviceGuard guard;
+  unsigned int status = 0;
+  if (cudaSetDevice(c->device) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(&status, c->xbuf + 8, sizeof(status), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return LOOM_STATUS_CUDA_ERROR;
+  return status == 0 ? LOOM_STATUS_OK : LOOM_STATUS_COMM_ERROR;
 }
 
 inline int nccl_group_start() { return ncclGroupStart() == ncclSuccess ? 0 : 1; }
@@ -201,14 +401,170 @@ inline int dist_finish<MaxOp>(void*, int64_t, float*, Comm*, cudaStream_t) {
   return LOOM_STATUS_OK;
 }
 
+// ---------------------------------------------------------------------------
+// peer-memory exchange
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ unsigned long long acc_bits(double v) {
+  return (unsigned long long)__double_as_longlong(v);
+}
+__device__ __forceinline__ unsigned long long acc_bits(float v) { return __float_as_uint(v); }
+template <class Acc>
+__device__ __forceinline__ Acc bits_acc(unsigned long long b);
+template <>
+__device__ __forceinline__ double bits_acc<double>(unsigned long long b) {
+  return __longlong_as_double((long long)b);
+}
+template <>
+__device__ __forceinline__ float bits_acc<float>(unsigned long long b) {
+  return __uint_as_float((unsigned int)b);
+}
+
+// One thread: take this rank's value (written by the local phase), store it
+// into slot [epoch parity][rank] of every rank's exchange buffer (value,
+// then the epoch with release semantics), then read the nranks values of
+// this epoch from the own buffer (acquire on the epoch) and fold them in
+// rank order into out[0].  The epoch is this rank's own exchange count, kept
+// in device memory, so the kernel also works when replayed from a graph.
+// A wait for a peer's value gives up after the communicator's timeout (30 s
+// unless set), records status 1 in the rank's own exchange buffer and
+// leaves NaN in out[0].  As a backstop that does not depend on the clock, it
+// also gives up after timeout / 16 polls: every poll is an uncached load of
+// far more than 16 ns.
+template <class Op>
+__global__ void peer_exchange_kernel(const typename Op::Acc* __restrict__ local,
+                                     const PeerTable peers, const int nranks, const int rank,
+                                     unsigned char* __restrict__ own, float* __restrict__ out,
+                                     const unsigned long long timeout_ns) {
+  using Acc = typename Op::Acc;
+  wait_for_prerequisite_grid();
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  unsigned long long* counter = reinterpret_cast<unsigned long long*>(own);
+  unsigned int* status = reinterpret_cast<unsigned int*>(own + 8);
+  const unsigned long long epoch = *counter + 1;
+  *counter = epoch;
+  const int set = (int)(epoch & 1ull) * kMaxRanks;
+  const unsigned long long bits = acc_bits(*local);
+  for (int r = 0; r < nranks; ++r) {
+    ExchangeSlot* s =
+        reinterpret_cast<ExchangeSlot*>(peers.buf[r] + kExchangeSlotsOffset) + set + rank;
+    st_relaxed_sys(&s->bits, bits);
+    st_release_sys(&s->epoch, epoch);
+  }
+  ExchangeSlot* mine = reinterpret_cast<ExchangeSlot*>(own + kExchangeSlotsOffset) + set;
+  Acc total = Op::init();
+  const unsigned long long t0 = global_ns();
+  const unsigned long long max_polls = timeout_ns / 16 + 1;
+  unsigned long long polls = 0;
+  for (int r = 0; r < nranks; ++r) {
+    while (ld_acquire_sys(&mine[r].epoch) != epoch) {
+      if (++polls > max_polls || global_ns() - t0 > timeout_ns) {
+        atomicExch(status, 1u);
+        out[0] = __int_as_float(0x7fffffff);  // NaN: no result
+        return;
+      }
+      __nanosleep(32);
+    }
+    total = Op::combine(total, bits_acc<Acc>(ld_relaxed_sys(&mine[r].bits)));
+  }
+  out[0] = Op::to_float(total);
+}
+
+// The exchange kernel as a programmatic dependent of the local phase (its
+// griddepcontrol.wait holds it until that phase has finished); a plain
+// launch where the attribute is refused.
+template <class Op>
+inline int launch_peer_exchange(void* workspace, int64_t n_local, float* out, Comm* comm,
+                                cudaStream_t stream) {
+  RankSlots<Op> slots(workspace, n_local);
+  const typename Op::Acc* local = slots.local;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, peer_exchange_kernel<Op>, local, comm->peers, comm->nranks,
+                         comm->rank, comm->xbuf, out, comm->timeout_ns) == cudaSuccess)
+    return LOOM_STATUS_OK;
+  cudaGetLastError();
+  peer_exchange_kernel<Op><<<1, 32, 0, stream>>>(local, comm->peers, comm->nranks, comm->rank,
+                                                 comm->xbuf, out, comm->timeout_ns);
+  return launch_status();
+}
+
 template <class Op, class Body>
 inline int dist_reduce(const Ptrs<Body::kInputs>& in, int64_t n_local, const Body& body,
                        void* workspace, float* out, Comm* comm, cudaStream_t stream) {
   int st = dist_local<Op>(in, n_local, body, workspace, stream);
   if (st != LOOM_STATUS_OK) return st;
+  if (comm->peer_exchange) return launch_peer_exchange<Op>(workspace, n_local, out, comm, stream);
   st = dist_collective<Op>(workspace, n_local, out, comm, stream);
   if (st != LOOM_STATUS_OK) return st;
   return dist_finish<Op>(workspace, n_local, out, comm, stream);
+}
+
+// One process, ndev GPUs, after the local phase on every device: the peer
+// exchange on every device (launched one device after another; each waits
+// for the others), or one grouped NCCL collective and the rank fold.
+template <class Op>
+inline int multi_exchange(int ndev, void* const* comms, void* const* workspace,
+                          const int64_t* shard_n, float* const* out) {
+  bool peer = true;
+  for (int d = 0; d < ndev; ++d) peer = peer && static_cast<Comm*>(comms[d])->peer_exchange;
+  if (peer) {
+    for (int d = 0; d < ndev; ++d) {
+      Comm* c = static_cast<Comm*>(comms[d]);
+      if (cudaSetDevice(c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;
+      const int st = launch_peer_exchange<Op>(workspace[d], shard_n[d], out[d], c, nullptr);
+      if (st != LOOM_STATUS_OK) return st;
+    }
+    return LOOM_STATUS_OK;
+  }
+  if (nccl_group_start() != 0) return LOOM_STATUS_COMM_ERROR;
+  int group_status = LOOM_STATUS_OK;
+  for (int d = 0; d < ndev && group_status == LOOM_STATUS_OK; ++d) {
+    group_status = dist_collective<Op>(workspace[d], shard_n[d], out[d],
+                                       static_cast<Comm*>(comms[d]), nullptr);
+  }
+  if (nccl_group_end() != 0) return LOOM_STATUS_COMM_ERROR;
+  if (group_status != LOOM_STATUS_OK) return group_status;
+  for (int d = 0; d < ndev; ++d) {
+    Comm* c = static_cast<Comm*>(comms[d]);
+    if (cudaSetDevice(c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;
+    const int st = dist_finish<Op>(workspace[d], shard_n[d], out[d], c, nullptr);
+    if (st != LOOM_STATUS_OK) return st;
+  }
+  return LOOM_STATUS_OK;
 }
 
 }  // namespace loomb

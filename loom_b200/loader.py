@@ -365,13 +365,41 @@ class Entry:
 
 
 class Comm:
-    """An NCCL communicator owned by a package (one rank of one process)."""
+    """A communicator owned by a package (one rank of one process): NCCL,
+    plus the peer-memory scalar exchange where every GPU reaches the
+    others' memory."""
 
     def __init__(self, package: "Package", handle: int, nranks: int, rank: int):
         self.package = package
         self.handle = handle
         self.nranks = nranks
         self.rank = rank
+
+    @property
+    def peer_exchange(self) -> bool:
+        """Whether reductions exchange their scalar through peer memory."""
+        return bool(self.package._comm_peer_exchange(ctypes.c_void_p(self.handle)))
+
+    def set_peer_exchange(self, enable: bool) -> None:
+        """Switch between the peer-memory exchange and NCCL.  Every rank
+        must make the same choice before its next reduction."""
+        st = self.package._comm_set_peer_exchange(ctypes.c_void_p(self.handle), int(enable))
+        if st != 0:
+            raise LoomError(f"loom_{self.package.name}_comm_set_peer_exchange", st)
+
+    def set_timeout_ms(self, ms: int) -> None:
+        """How long a peer exchange waits for the other ranks before it gives
+        up (its result is then NaN and `check` raises)."""
+        st = self.package._comm_set_timeout_ms(ctypes.c_void_p(self.handle), int(ms))
+        if st != 0:
+            raise LoomError(f"loom_{self.package.name}_comm_set_timeout_ms", st)
+
+    def check(self) -> None:
+        """Wait for this rank's device; raise if a peer exchange gave up
+        waiting for another rank (its result was NaN)."""
+        st = self.package._comm_check(ctypes.c_void_p(self.handle))
+        if st != 0:
+            raise LoomError(f"loom_{self.package.name}_comm_check", st)
 
     def destroy(self) -> None:
         if self.handle:
@@ -409,6 +437,14 @@ class Package:
                                             ctypes.POINTER(ctypes.c_int)]
             self._comm_destroy = getattr(self.lib, prefix + "_destroy")
             self._comm_destroy.argtypes = [ctypes.c_void_p]
+            self._comm_set_peer_exchange = getattr(self.lib, prefix + "_set_peer_exchange")
+            self._comm_set_peer_exchange.argtypes = [ctypes.c_void_p, ctypes.c_int]
+            self._comm_set_timeout_ms = getattr(self.lib, prefix + "_set_timeout_ms")
+            self._comm_set_timeout_ms.argtypes = [ctypes.c_void_p, ctypes.c_int64]
+            self._comm_peer_exchange = getattr(self.lib, prefix + "_peer_exchange")
+            self._comm_peer_exchange.argtypes = [ctypes.c_void_p]
+            self._comm_check = getattr(self.lib, prefix + "_check")
+            self._comm_check.argtypes = [ctypes.c_void_p]
 
     def __getitem__(self, entry: str) -> Entry:
         return self.entries[entry]

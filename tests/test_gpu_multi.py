@@ -1,10 +1,15 @@
 """Multi-GPU entries against the oracle on the full (unsharded) input.
 
 * `_multi`: one process drives every visible GPU (up to 8), one contiguous
-  shard per device (`loom_b200.shard.shard_bounds`), one grouped NCCL
-  collective for reductions.
-* `_dist`: one process per GPU (2 ranks), the NCCL communicator's id
-  rendezvoused over a gloo process group.
+  shard per device (`loom_b200.shard.shard_bounds`); reductions exchange
+  their scalar through peer memory or, switched, one grouped NCCL
+  collective.
+* `_dist`: one process per GPU (2 ranks), the communicator's id rendezvoused
+  over a gloo process group; every reduction runs through both exchange
+  paths, which must give the same bits.
+* A bounded wait: a reduction launched on one rank only must give up after
+  its time limit, report it through `Comm.check`, and return NaN, leaving
+  the GPU usable.
 
 Maps must reproduce the oracle bit for bit once the shards are concatenated;
 reductions must give the same bits on every device, max exactly and sums to
@@ -45,11 +50,15 @@ def _check(entry, results, ref, full, n):
         check_sum(entry, got, ref, full, n)
 
 
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
 @pytest.mark.parametrize("n", [(1 << 22) + 3, 37, 3])
-def test_multi_one_process(suite_pkg, oracle, n):
+def test_multi_one_process(suite_pkg, oracle, n, exchange):
     devs = list(range(min(torch.cuda.device_count(), 8)))
     comms = suite_pkg.comm_init_all(devs)
     try:
+        assert all(c.peer_exchange for c in comms)    # NVLink: every pair reaches the others
+        for c in comms:
+            c.set_peer_exchange(exchange == "peer")
         bounds = shard_bounds(n, len(devs))
         for entry in ENTRIES:
             full = workloads.entry_inputs(entry, n, seed_offset=len(devs))
@@ -63,6 +72,8 @@ def test_multi_one_process(suite_pkg, oracle, n):
             _check(entry, results, oracle.run(entry, full), full, n)
             if entry not in MAPS:
                 assert host == results[0]
+        for c in comms:
+            c.check()
     finally:
         for c in comms:
             c.destroy()
@@ -89,14 +100,23 @@ def _dist_rank(rank, world, port, n, queue):
     try:
         pkg = load_suite()
         comm = pkg.comm_from_process_group()
+        assert comm.peer_exchange
         start, stop = shard_bounds(n, world)[rank]
         for entry in ENTRIES:
             full = workloads.entry_inputs(entry, n, seed_offset=world + 100)
             mine = {k: (torch.from_numpy(np.ascontiguousarray(v[start:stop])).cuda()
                         if isinstance(v, np.ndarray) else v) for k, v in full.items()}
-            out = pkg[entry].dist(comm, **mine)
-            torch.cuda.synchronize()
-            res = out.cpu().numpy() if entry in MAPS else float(out.cpu()[0])
+            runs = []
+            for peer in (True, False, True):
+                comm.set_peer_exchange(peer)
+                out = pkg[entry].dist(comm, **mine)
+                torch.cuda.synchronize()
+                runs.append(out.cpu().numpy())
+            comm.check()
+            # the same bits through peer memory, NCCL, and peer memory again
+            assert all(np.array_equal(r.view(np.uint32), runs[0].view(np.uint32))
+                       for r in runs), entry
+            res = runs[0] if entry in MAPS else float(runs[0][0])
             gathered = [None] * world
             dist.all_gather_object(gathered, res)
             if rank == 0:
@@ -126,3 +146,25 @@ def test_dist_one_process_per_gpu(oracle):
     for entry in ENTRIES:
         full = workloads.entry_inputs(entry, n, seed_offset=world + 100)
         _check(entry, got[entry], oracle.run(entry, full), full, n)
+
+
+def test_exchange_wait_is_bounded(suite_pkg):
+    # Only device 0 takes part: its exchange waits for a value that nobody
+    # sends, gives up after its time limit (1 s here), records the failure
+    # and returns NaN.  The device stays usable.
+    comms = suite_pkg.comm_init_all([0, 1])
+    try:
+        assert comms[0].peer_exchange
+        comms[0].set_timeout_ms(1000)
+        x = torch.ones(4096, device="cuda:0")
+        with torch.cuda.device(0):
+            out = suite_pkg["dot"].dist(comms[0], x=x, y=x)
+            torch.cuda.synchronize()
+        assert np.isnan(float(out.cpu()[0]))
+        with pytest.raises(Exception) as info:
+            comms[0].check()
+        assert info.value.status == 4          # LOOM_STATUS_COMM_ERROR
+        assert float(suite_pkg["dot"](x=x, y=x).cpu()[0]) == 4096.0
+    finally:
+        for c in comms:
+            c.destroy()
