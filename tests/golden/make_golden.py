@@ -37,7 +37,8 @@ def main(ref: str) -> None:
             ["saxpy", "relu", "dot", "l2_norm_sq", "max_value", "affine_relu", "pipeline_sum"],
         os.path.join(HERE, "sources", "cases", "frontend_cases.py"):
             ["nested_helpers", "clamp_scale", "tuple_lets", "soft_threshold", "hypot_sum",
-             "neg_max", "ratio_exp", "select_floor", "scaled_chain"],
+             "neg_max", "ratio_exp", "select_floor", "scaled_chain", "tail_if",
+             "qualified_prims", "unary_and_eq", "let_chain_sum", "max_of_difference"],
         os.path.join(ref, "examples", "saxpy.py"): ["saxpy"],
         os.path.join(ref, "examples", "relu.py"): ["relu"],
         os.path.join(ref, "examples", "dot.py"): ["dot"],
@@ -61,7 +62,8 @@ def main(ref: str) -> None:
     errors = {}
     bad = os.path.join(HERE, "sources", "errors", "frontend_errors.py")
     for entry in ("with_loop", "tensor_capture", "chained", "keyword_call", "wrong_return",
-                  "unknown_call", "tensor_branch"):
+                  "unknown_call", "tensor_branch", "power_op", "aug_assign", "non_tail_if",
+                  "bool_not", "attribute_access"):
         proc = subprocess.run([sys.executable, frontend, "front-ir-json", bad, "--entry", entry],
                               capture_output=True, text=True)
         errors[entry] = {"returncode": proc.returncode,

@@ -1,8 +1,11 @@
 """Loom entries written for the front-end and body-coverage tests: local
 helper functions passed to maps and applied, tuple lets, annotated lets, clamps,
-soft thresholds, square roots, exp/log, division, select, negation and a
-max of a map.  (Its FrontIR from the reference frontend is committed under
+soft thresholds, square roots, exp/log, division, select, negation, a tail
+if statement, qualified primitives (math.sqrt, loom.max ...), unary plus and
+equality, and maxes of maps.  (Its FrontIR from the reference frontend is committed under
 tests/golden/front_ir/; tests/golden/make_golden.py regenerates it.)"""
+
+import math
 
 import loom
 
@@ -68,3 +71,41 @@ def scaled_chain(a: float, x: loom.Tensor1, y: loom.Tensor1, w: loom.Tensor1) ->
     d = loom.Tensor1.map2(affine, x, y)
     sq = loom.Tensor1.map(lambda di: di * di, d)
     return loom.Tensor1.reduce_sum(loom.Tensor1.map2(lambda s_, wi: s_ / (wi * wi + 1.0), sq, w))
+
+
+@loom.entry
+def tail_if(k: float, x: loom.Tensor1) -> loom.Tensor1:
+    def gate(v: float) -> float:
+        if v > k:
+            return v - k
+        else:
+            return 0.0
+
+    return loom.Tensor1.map(gate, x)
+
+
+@loom.entry
+def qualified_prims(x: loom.Tensor1, y: loom.Tensor1) -> loom.Tensor1:
+    return loom.Tensor1.map2(
+        lambda xi, yi: loom.select(xi <= yi, math.sqrt(xi * xi + 1.0),
+                                   loom.max(xi, yi) - loom.min(yi, 0.5)), x, y)
+
+
+@loom.entry
+def unary_and_eq(x: loom.Tensor1) -> loom.Tensor1:
+    return loom.Tensor1.map(lambda xi: select(xi == 0.0, +xi, -xi * 0.5), x)
+
+
+@loom.entry
+def let_chain_sum(a: float, x: loom.Tensor1) -> float:
+    def f(v: float) -> float:
+        u: float = v * a
+        w = u - 1.0
+        return u * w
+
+    return loom.Tensor1.reduce_sum(loom.Tensor1.map(f, x))
+
+
+@loom.entry
+def max_of_difference(x: loom.Tensor1, y: loom.Tensor1) -> float:
+    return loom.Tensor1.reduce_max(loom.Tensor1.map2(lambda xi, yi: xi - yi, x, y))

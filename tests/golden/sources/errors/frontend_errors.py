@@ -42,3 +42,37 @@ def tensor_branch(x: loom.Tensor1, k: float) -> loom.Tensor1:
         return loom.Tensor1.map(lambda xi: xi * k, x)
     else:
         return loom.Tensor1.map(lambda xi: xi, x)
+
+
+@loom.entry
+def power_op(x: loom.Tensor1) -> loom.Tensor1:
+    return loom.Tensor1.map(lambda xi: xi ** 2.0, x)
+
+
+@loom.entry
+def aug_assign(a: float, x: loom.Tensor1) -> loom.Tensor1:
+    b = a
+    b += 1.0
+    return loom.Tensor1.map(lambda xi: xi * b, x)
+
+
+@loom.entry
+def non_tail_if(a: float, x: loom.Tensor1) -> loom.Tensor1:
+    def f(v: float) -> float:
+        if v > a:
+            w = v
+        else:
+            w = a
+        return w
+
+    return loom.Tensor1.map(f, x)
+
+
+@loom.entry
+def bool_not(x: loom.Tensor1) -> loom.Tensor1:
+    return loom.Tensor1.map(lambda xi: select(not (xi > 0.0), xi, 0.0), x)
+
+
+@loom.entry
+def attribute_access(x: loom.Tensor1) -> loom.Tensor1:
+    return loom.Tensor1.map(lambda xi: xi * x.shape, x)

@@ -1,6 +1,7 @@
 """Broader bodies through the whole pipeline (Python source -> front end ->
 B200 package -> CUDA) against the oracle: helper functions, clamps, soft
-thresholds, sqrt, exp/log, division, select, negation, a max over a map and
+thresholds, sqrt, exp/log, division, select, negation, a tail if statement,
+qualified primitives, unary plus and equality, maxes over maps and
 multi-node chains (tests/golden/sources/cases/frontend_cases.py).
 
 The project is packaged twice: with the reference's default flags, and with
@@ -34,7 +35,7 @@ pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CASES = os.path.join(HERE, "golden", "sources", "cases")
-SCALARS = {"lo": -0.5, "hi": 0.75, "s": 1.5, "a": 0.3, "t": 0.25}
+SCALARS = {"lo": -0.5, "hi": 0.75, "s": 1.5, "a": 0.3, "t": 0.25, "k": 0.4}
 SCALARS_BY_ENTRY = {"scaled_chain": {"a": 1.25}}
 
 
@@ -62,6 +63,9 @@ def _values(entry, inp):
     if entry == "scaled_chain":
         d = inp["a"] * x - y
         return d * d / (inp["w"].astype(np.float64) ** 2 + 1.0)
+    if entry == "let_chain_sum":
+        u = x * inp["a"]
+        return u * (u - 1.0)
     raise KeyError(entry)
 
 
