@@ -42,6 +42,13 @@ GENCODE = "arch=compute_100a,code=sm_100a"
 HONOURED_FLAGS = {"cuda-async-wrapper-return", "cuda-pointwise-tail-tune",
                   "cuda-pointwise-predicated-select", "cuda-pointwise-selected-tail-plan",
                   "cuda-body-trait-analysis", "shared-body-trait-analysis"}
+# The TensorIR fusion passes and the policy flags that steer them, which the
+# Python front end applies to Python sources (frontend/passes.py); TensorIR
+# files are taken as given, as `loomc` ran its passes before writing them.
+FRONTEND_PASS_FLAGS = {"map-chain-collapse", "elementwise-fusion", "small-producer-clone",
+                       "reduce-map-fusion", "shape-use-simplify", "materialization-choice",
+                       "reduction-materialization-choice", "reduction-late-fusion-guard",
+                       "branch-aware-fusion-guard", "pointwise-materialization-guard"}
 
 
 class BuildError(RuntimeError):
@@ -63,9 +70,11 @@ class Options:
         return "cuda-async-wrapper-return" in self.enabled
 
     def to_json(self) -> dict:
-        return {"enabled": sorted(set(self.enabled)),
-                "honoured": sorted(set(self.enabled) & HONOURED_FLAGS),
-                "no_effect_on_b200_plan": sorted(set(self.enabled) - HONOURED_FLAGS)}
+        on = set(self.enabled)
+        return {"enabled": sorted(on),
+                "honoured": sorted(on & HONOURED_FLAGS),
+                "tensor_ir_passes_for_python_sources": sorted(on & FRONTEND_PASS_FLAGS),
+                "no_effect_on_b200_plan": sorted(on - HONOURED_FLAGS - FRONTEND_PASS_FLAGS)}
 
 
 @dataclass
@@ -99,12 +108,13 @@ def _defines_entries(path: str) -> bool:
     return "loom.entry" in text or "@entry" in text
 
 
-def load_source_file(path: str) -> List[Program]:
-    """Programs of one source: a ``*.tensor_ir.json`` (one program or a list)
-    or a Python module of ``@loom.entry`` functions (through the front end)."""
+def load_source_file(path: str, enabled: Sequence[str] = ()) -> List[Program]:
+    """Programs of one source: a ``*.tensor_ir.json`` (one program or a list,
+    taken as given) or a Python module of ``@loom.entry`` functions (through
+    the front end, with the TensorIR passes `enabled` switches on)."""
     if path.endswith(".py"):
         from .frontend import python_programs
-        return python_programs(path)
+        return python_programs(path, enabled)
     return load_entries_file(path)
 
 
@@ -129,7 +139,7 @@ def discover_entries(project_root: str, module_filters: Sequence[str] = (),
         module = module_name_of_file(path)
         if mfilt and module.lower() not in mfilt:
             continue
-        for prog in load_source_file(path):
+        for prog in load_source_file(path, enabled):
             if efilt and prog.entry_name.lower() not in efilt:
                 continue
             bundles.append(EntryBundle(module, path, prog, plan_entry(prog, module, enabled)))
@@ -366,7 +376,8 @@ def compile_entry(source_file: str, entry_name: str, out_dir: str,
     """``loomc compile <file> --entry e --target cuda`` (cuda_backend.ml:2675-2731)."""
     opts = opts or Options()
     module = module_name_of_file(source_file)
-    progs = [p for p in load_source_file(source_file) if p.entry_name == entry_name]
+    progs = [p for p in load_source_file(source_file, opts.enabled)
+             if p.entry_name == entry_name]
     if not progs:
         raise TensorIRError(f"entry {entry_name!r} not found in {source_file}")
     prog = progs[0]

@@ -23,6 +23,8 @@ SUITE_DIR = os.path.join(BUILT_DIR, "b200_suite")
 
 # Reference flags that change how map bodies are rendered; the body-coverage
 # test project is also packaged with them (as frontend_cases_flags).
+# the reference's TensorIR fusion passes (restated in loom_b200/frontend/passes.py)
+FUSION_FLAGS = ["map-chain-collapse", "reduce-map-fusion", "shape-use-simplify"]
 RENDER_FLAGS = ["cuda-pointwise-tail-tune", "cuda-pointwise-predicated-select",
                 "cuda-pointwise-selected-tail-plan", "cuda-body-trait-analysis"]
 

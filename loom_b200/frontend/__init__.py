@@ -11,11 +11,12 @@ from .lower import loom_lambda, program_from_front_ir, tensor_ir
 from .python_front import FrontendError, front_ir, list_entries
 
 
-def python_programs(path: str) -> List[TI.Program]:
-    """Every ``@loom.entry`` of a Python source file, lowered to TensorIR."""
+def python_programs(path: str, enabled=()) -> List[TI.Program]:
+    """Every ``@loom.entry`` of a Python source file, lowered to TensorIR
+    (with the TensorIR passes that the flags in `enabled` switch on)."""
     with open(path, "r", encoding="utf-8") as fh:
         src = fh.read()
-    return [program_from_front_ir(front_ir(src, e["name"], path))
+    return [program_from_front_ir(front_ir(src, e["name"], path), enabled)
             for e in list_entries(src, path)]
 
 

@@ -388,7 +388,11 @@ def _use_counts(prog: TI.Program) -> Dict[int, int]:
     return counts
 
 
-def annotate(prog: TI.Program) -> TI.Program:
+def annotate(prog: TI.Program, enabled=()) -> TI.Program:
+    """Metrics, reduction shapes and handling hints of every node
+    (tensor_passes.ml:513-548); the hints depend on the materialisation flags
+    in `enabled`."""
+    from .passes import materialization_hint
     uses = _use_counts(prog)
     for n in prog.nodes:
         u = uses.get(n.id, 0)
@@ -406,12 +410,15 @@ def annotate(prog: TI.Program) -> TI.Program:
                 n.reduction_shape = ("branchy-mapped" if has_sel else "ratio-mapped" if has_div
                                      else "weighted-mapped" if n.source.scalar_params
                                      else "mapped")
-        n.handling_hint = "no-preference"
+        n.handling_hint = materialization_hint(
+            enabled, n.metrics, None if isinstance(n, TI.Elementwise1D) else n.reduction_shape)
     return prog
 
 
-def tensor_ir(lam: dict) -> TI.Program:
-    """LoomLambda entry -> annotated, validated TensorIR program."""
+def tensor_ir(lam: dict, enabled=()) -> TI.Program:
+    """LoomLambda entry -> annotated, validated TensorIR program, after the
+    restated TensorIR passes that `enabled` switches on (passes.py)."""
+    from .passes import apply_tensor_passes
     env = {}
     params: List[TI.Param] = []
     for p in lam["params"]:
@@ -433,10 +440,11 @@ def tensor_ir(lam: dict) -> TI.Program:
         raise FrontendError("entry lowered to a scalar expression instead of a reduction result")
     prog = TI.Program(entry_name=lam["entry"], params=params, result_kind=kind, result=ref,
                       nodes=tz.nodes)
-    annotate(prog)
+    prog = apply_tensor_passes(prog, enabled)
+    annotate(prog, enabled)
     TI.validate(prog)
     return prog
 
 
-def program_from_front_ir(front: dict) -> TI.Program:
-    return tensor_ir(loom_lambda(front))
+def program_from_front_ir(front: dict, enabled=()) -> TI.Program:
+    return tensor_ir(loom_lambda(front), enabled)

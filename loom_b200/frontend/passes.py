@@ -1,0 +1,278 @@
+"""The reference's TensorIR fusion passes, for the Python front end.
+
+`loomc` runs these after tensorization when their flags are enabled
+(``src/loom_tensorize/tensor_passes.ml:595-620``); with them the TensorIR
+that reaches a backend has producer maps folded into their consumers:
+
+* ``fuse_program`` (``tensor_passes.ml:130-232``) -- under
+  ``map-chain-collapse``, ``elementwise-fusion`` or ``small-producer-clone``:
+  an element-wise producer is substituted into an element-wise consumer's
+  body, its inputs renamed ``<binding>__<input>__f<i>``;
+* ``reduce_map_fusion_program`` (``:251-335``) -- under
+  ``reduce-map-fusion``: a reduction over an element-wise node becomes a
+  mapped reduction (``MappedInput``), inputs renamed ``<input>__r<i>``;
+* ``shape_use_simplify`` (``:103-112``) -- under ``shape-use-simplify``: nodes
+  the result does not reach are dropped;
+
+each gated by the materialisation policy
+(``src/loom_tensorize/materialization_policy.ml:1-94``), and the handling
+hints that annotation attaches (``materialization_hint``, ``:1-44``).  The
+thresholds are the reference's defaults (``configs/optimizations/current.json``).
+
+The B200 plan inlines every element-wise chain into one kernel whether or
+not these passes ran, so they change the TensorIR (and its dump under
+``entries/``), not the kernels; what they can change is which rendering
+flags apply to a body, since a body fused into a reduction renders with the
+defaults.  The reference's other TensorIR passes (CSE, canonicalisation,
+reduction-body rewrites) are not restated.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Sequence, Tuple
+
+from .. import tensor_ir as TI
+from .lower import _use_counts, body_metrics
+
+# configs/optimizations/current.json (the reference's defaults)
+SMALL_CLONE_NODES = 12
+BRANCHY_FUSION_COMPLEXITY = 6
+POINTWISE_MATERIALIZATION_COMPLEXITY = 5
+MATERIALIZE_MULTI_USE_COMPLEXITY = 4
+REDUCTION_BODY_CSE_MIN_OCCURRENCES = 2
+REDUCTION_MATERIALIZE_COMPLEXITY = 5
+REDUCTION_LATE_FUSION_COMPLEXITY = 8
+
+FUSE_FLAGS = ("map-chain-collapse", "elementwise-fusion", "small-producer-clone")
+
+
+def _on(enabled: Sequence[str], flag: str) -> bool:
+    return flag in enabled
+
+
+# --- materialisation policy (materialization_policy.ml) -----------------------
+
+def allow_inline_producer(enabled, m: TI.BodyMetrics, use_count: int) -> str:
+    """"fuse", "clone" or "disallow" for an element-wise producer
+    (materialization_policy.ml:46-68)."""
+    branch_guard = (_on(enabled, "branch-aware-fusion-guard") and m.has_branch
+                    and m.scalar_complexity >= BRANCHY_FUSION_COMPLEXITY)
+    pointwise_guard = (_on(enabled, "pointwise-materialization-guard")
+                       and (m.has_branch or m.has_div)
+                       and m.scalar_complexity >= POINTWISE_MATERIALIZATION_COMPLEXITY)
+    if branch_guard or pointwise_guard:
+        return "disallow"
+    if use_count <= 1:
+        return "fuse"
+    if (_on(enabled, "materialization-choice")
+            and m.scalar_complexity >= MATERIALIZE_MULTI_USE_COMPLEXITY):
+        return "disallow"
+    return "clone"
+
+
+def allow_inline_into_reduction(enabled, m: TI.BodyMetrics, use_count: int,
+                                target_complexity: int) -> str:
+    """The same decision for a producer feeding a reduction
+    (materialization_policy.ml:70-94)."""
+    late_guard = _on(enabled, "reduction-late-fusion-guard") and (
+        m.scalar_complexity + target_complexity >= REDUCTION_LATE_FUSION_COMPLEXITY
+        or (m.has_branch and target_complexity > 0)
+        or m.repeated_subexpressions >= REDUCTION_BODY_CSE_MIN_OCCURRENCES)
+    if late_guard:
+        return "disallow"
+    if (_on(enabled, "reduction-materialization-choice")
+            and (m.scalar_complexity >= REDUCTION_MATERIALIZE_COMPLEXITY or m.has_branch
+                 or m.div_count > 0)
+            and use_count > 1):
+        return "disallow"
+    return allow_inline_producer(enabled, m, use_count)
+
+
+def materialization_hint(enabled, m: TI.BodyMetrics, reduction_shape) -> str:
+    """The handling hint annotation attaches to a node
+    (materialization_policy.ml:1-44)."""
+    if not _on(enabled, "materialization-choice"):
+        return "no-preference"
+    if reduction_shape is not None and _on(enabled, "reduction-materialization-choice"):
+        if reduction_shape == "branchy-mapped":
+            return "prefer-materialize"
+        if reduction_shape == "ratio-mapped" and (
+                m.scalar_complexity >= REDUCTION_MATERIALIZE_COMPLEXITY or m.div_count > 0):
+            return "prefer-materialize"
+        if reduction_shape == "weighted-mapped" and (
+                m.repeated_subexpressions > 0 or m.estimated_uses > 1):
+            return "prefer-clone"
+        if m.estimated_uses <= 1:
+            return "prefer-fuse"
+        if (m.scalar_complexity >= REDUCTION_MATERIALIZE_COMPLEXITY
+                or m.repeated_subexpressions > 0):
+            return "prefer-materialize"
+        return "prefer-clone"
+    if reduction_shape == "branchy-mapped":
+        return "prefer-materialize"
+    if reduction_shape == "ratio-mapped" and m.scalar_complexity >= 3:
+        return "prefer-materialize"
+    if m.estimated_uses <= 1:
+        return "prefer-fuse"
+    if m.scalar_complexity <= SMALL_CLONE_NODES:
+        return "prefer-clone"
+    if m.has_branch or m.scalar_complexity >= MATERIALIZE_MULTI_USE_COMPLEXITY:
+        return "prefer-materialize"
+    return "prefer-clone"
+
+
+# --- expression helpers (reduction_analysis.ml:376-396) ------------------------
+
+def substitute(name: str, replacement, e):
+    if isinstance(e, TI.SVar):
+        return replacement if e.name == name else e
+    if isinstance(e, TI.SUnary):
+        return TI.SUnary(e.op, substitute(name, replacement, e.expr))
+    if isinstance(e, TI.SBinary):
+        return TI.SBinary(e.op, substitute(name, replacement, e.lhs),
+                          substitute(name, replacement, e.rhs))
+    if isinstance(e, TI.SSelect):
+        return TI.SSelect(substitute(name, replacement, e.cond),
+                          substitute(name, replacement, e.then),
+                          substitute(name, replacement, e.els))
+    return e
+
+
+def rename_vars(renamings: List[Tuple[str, str]], e):
+    """Applies the renamings one after another, as the reference does."""
+    for old, new in renamings:
+        e = substitute(old, TI.SVar(new), e)
+    return e
+
+
+def _fresh(base: str, suffix: str, existing: Sequence[TI.InputBinding]) -> str:
+    names = {b.name for b in existing}
+    i = 0
+    while f"{base}__{suffix}{i}" in names:
+        i += 1
+    return f"{base}__{suffix}{i}"
+
+
+# --- the passes -----------------------------------------------------------------
+
+def fuse_program(prog: TI.Program, enabled, allow_clone: bool = False,
+                 clone_limit: int = SMALL_CLONE_NODES) -> TI.Program:
+    """Element-wise producers into element-wise consumers
+    (tensor_passes.ml:130-232)."""
+    uses = _use_counts(prog)
+    done: Dict[int, TI.Elementwise1D] = {}
+    fused = set()
+    nodes = []
+    for node in prog.nodes:
+        if not isinstance(node, TI.Elementwise1D):
+            done[node.id] = node
+            nodes.append(node)
+            continue
+        inputs: List[TI.InputBinding] = []
+        body = node.body
+        scalars = list(node.scalar_params)
+        for b in node.inputs:
+            producer = done.get(b.source.id) if isinstance(b.source, TI.NodeRef) else None
+            use_count = uses.get(b.source.id) if isinstance(b.source, TI.NodeRef) else None
+            if not isinstance(producer, TI.Elementwise1D) or use_count is None:
+                inputs.append(b)
+                continue
+            decision = allow_inline_producer(enabled, body_metrics(use_count, producer.body),
+                                             use_count)
+            if decision == "disallow" or (
+                    decision == "clone"
+                    and (not allow_clone or TI.complexity(producer.body) > clone_limit)):
+                inputs.append(b)
+                continue
+            if use_count == 1:
+                fused.add(producer.id)
+            renamed, renamings = [], []
+            for pi in producer.inputs:
+                fresh = _fresh(f"{b.name}__{pi.name}", "f", inputs + renamed)
+                renamed.append(TI.InputBinding(fresh, pi.source))
+                renamings.append((pi.name, fresh))
+            body = substitute(b.name, rename_vars(renamings, producer.body), body)
+            inputs = inputs + renamed
+            scalars = sorted(set(scalars) | set(producer.scalar_params))
+        new = TI.Elementwise1D(node.id, tuple(inputs), tuple(scalars), body,
+                               shape_symbol=node.shape_symbol, metrics=node.metrics,
+                               handling_hint=node.handling_hint)
+        done[node.id] = new
+        nodes.append(new)
+    prog.nodes = [n for n in nodes if n.id not in fused]
+    return prog
+
+
+def reduce_map_fusion_program(prog: TI.Program, enabled, allow_clone: bool = False,
+                              clone_limit: int = SMALL_CLONE_NODES) -> TI.Program:
+    """A reduction over an element-wise node becomes a mapped reduction
+    (tensor_passes.ml:251-335)."""
+    uses = _use_counts(prog)
+    by_id = {n.id: n for n in prog.nodes}
+    fused = set()
+    nodes = []
+    for node in prog.nodes:
+        src = node.source if isinstance(node, TI.Reduce1D) else None
+        if not (isinstance(src, TI.PlainInput) and isinstance(src.input, TI.NodeRef)):
+            nodes.append(node)
+            continue
+        producer = by_id.get(src.input.id)
+        use_count = uses.get(src.input.id)
+        if not isinstance(producer, TI.Elementwise1D) or use_count is None:
+            nodes.append(node)
+            continue
+        decision = allow_inline_into_reduction(
+            enabled, body_metrics(use_count, producer.body), use_count, 0)
+        if decision == "disallow" or (
+                decision == "clone"
+                and (not allow_clone or TI.complexity(producer.body) > clone_limit)):
+            nodes.append(node)
+            continue
+        if use_count == 1:
+            fused.add(producer.id)
+        inputs, renamings = [], []
+        for b in producer.inputs:
+            fresh = _fresh(b.name, "r", inputs + list(producer.inputs))
+            inputs.append(TI.InputBinding(fresh, b.source))
+            renamings.append((b.name, fresh))
+        node.source = TI.MappedInput(tuple(inputs), tuple(producer.scalar_params),
+                                     rename_vars(renamings, producer.body))
+        nodes.append(node)
+    prog.nodes = [n for n in nodes
+                  if not (isinstance(n, TI.Elementwise1D) and n.id in fused)]
+    return prog
+
+
+def shape_use_simplify(prog: TI.Program) -> TI.Program:
+    """Drop the nodes the result does not reach (tensor_passes.ml:65-112)."""
+    by_id = {n.id: n for n in prog.nodes}
+    seen = set()
+    stack = [prog.result]
+    while stack:
+        ref = stack.pop()
+        if not isinstance(ref, TI.NodeRef) or ref.id in seen:
+            continue
+        seen.add(ref.id)
+        n = by_id.get(ref.id)
+        if isinstance(n, TI.Elementwise1D):
+            stack.extend(b.source for b in n.inputs)
+        elif isinstance(n, TI.Reduce1D):
+            if isinstance(n.source, TI.PlainInput):
+                stack.append(n.source.input)
+            else:
+                stack.extend(b.source for b in n.source.inputs)
+    prog.nodes = [n for n in prog.nodes if n.id in seen]
+    return prog
+
+
+def apply_tensor_passes(prog: TI.Program, enabled: Sequence[str]) -> TI.Program:
+    """The restated passes in the reference's order (tensor_passes.ml:595-620)."""
+    enabled = tuple(enabled)
+    clone = _on(enabled, "small-producer-clone")
+    if any(_on(enabled, f) for f in FUSE_FLAGS):
+        prog = fuse_program(prog, enabled, allow_clone=clone)
+    if _on(enabled, "reduce-map-fusion"):
+        prog = reduce_map_fusion_program(prog, enabled, allow_clone=clone)
+    if _on(enabled, "shape-use-simplify"):
+        prog = shape_use_simplify(prog)
+    return prog

@@ -25,7 +25,7 @@ import pytest
 import torch
 
 from loom_b200 import tensor_ir as TI
-from loom_b200.build import RENDER_FLAGS, build_project
+from loom_b200.build import FUSION_FLAGS, RENDER_FLAGS, build_project
 from loom_b200.frontend import python_programs
 from loom_b200.loader import Package
 
@@ -39,17 +39,26 @@ SCALARS = {"lo": -0.5, "hi": 0.75, "s": 1.5, "a": 0.3, "t": 0.25, "k": 0.4}
 SCALARS_BY_ENTRY = {"scaled_chain": {"a": 1.25}}
 
 
-@pytest.fixture(scope="module", params=["default", "render_flags"])
+@pytest.fixture(scope="module", params=["default", "render_flags", "fusion"])
 def cases(request):
     from oracle.loom_oracle import Oracle
-    progs = python_programs(os.path.join(CASES, "frontend_cases.py"))
+    src = os.path.join(CASES, "frontend_cases.py")
     if request.param == "default":
+        progs = python_programs(src)
         pkg = Package(build_project(CASES))
         oracle = Oracle([TI.program_to_json(p) for p in progs], name="frontend_cases")
-    else:
+    elif request.param == "render_flags":
+        progs = python_programs(src)
         pkg = Package(build_project(CASES, enabled=RENDER_FLAGS, name="frontend_cases_flags"))
         oracle = Oracle([TI.program_to_json(p) for p in progs], name="frontend_cases_flags",
                         enabled=RENDER_FLAGS)
+    else:
+        # the reference's TensorIR fusion passes ahead of the backend: the
+        # oracle evaluates the same fused programs
+        progs = python_programs(src, FUSION_FLAGS)
+        pkg = Package(build_project(CASES, enabled=FUSION_FLAGS, name="frontend_cases_fused"))
+        oracle = Oracle([TI.program_to_json(p) for p in progs], name="frontend_cases_fused",
+                        enabled=FUSION_FLAGS)
     return pkg, oracle, {p.entry_name: p for p in progs}
 
 
@@ -94,7 +103,7 @@ def test_bodies_match_oracle(cases, n, offset):
                 np.testing.assert_allclose(got, ref, rtol=1e-6, atol=0)
             else:
                 assert_bits(got, ref)
-        elif prog.nodes[prog.result.id].kind == "max":
+        elif prog.node(prog.result.id).kind == "max":
             assert float(got[0]) == float(np.float32(ref)), entry
         else:
             v = _values(entry, inp)
