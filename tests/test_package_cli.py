@@ -139,3 +139,44 @@ def test_package_shared_library_runtime(shared_package):
     ws = torch.empty(size, device="cuda", dtype=torch.uint8)
     assert dot(ptr(x), ptr(y), n, ptr(s), ptr(ws), size) == 0
     torch.testing.assert_close(s[0], torch.sum(x * y), rtol=1e-4, atol=1e-5)
+
+
+@pytest.fixture(scope="module")
+def async_package(tmp_path_factory):
+    tmp = tmp_path_factory.mktemp("pkg_async")
+    proj = _project(tmp)
+    out = tmp / "out"
+    result = _package("--project", str(proj), "--out", str(out),
+                      "--enable-opt", "cuda-async-wrapper-return")
+    assert result.returncode == 0, result.stderr
+    return out
+
+
+def test_async_wrapper_return_drops_the_final_synchronise(async_package, shared_package):
+    # cuda_backend.ml:2263-2267: with cuda-async-wrapper-return the plain entry
+    # returns right after its launches instead of synchronising the device
+    manifest = json.loads((async_package / "manifest.json").read_text())
+    assert manifest["optimizations"]["honoured"] == ["cuda-async-wrapper-return"]
+    src = (async_package / "src-gen" / "package_project.cu").read_text()
+    sync_src = (shared_package / "src-gen" / "package_project.cu").read_text()
+
+    def plain_entry(text, name):
+        start = text.index(f'extern "C" int loom_kernels_{name}(')
+        return text[start:text.index("\n}\n", start)]
+
+    for name in ("saxpy", "dot"):
+        assert "finish_sync" in plain_entry(sync_src, name)
+        assert "finish_sync" not in plain_entry(src, name)
+
+
+@pytest.mark.gpu
+def test_async_wrapper_return_results_after_synchronise(async_package):
+    import torch
+    from loom_b200.loader import Package
+    pkg = Package(str(async_package))
+    x = torch.randn(1 << 20, device="cuda")
+    y = torch.randn(1 << 20, device="cuda")
+    s = pkg["dot"](x=x, y=y)          # the plain entry: returns without synchronising
+    torch.cuda.synchronize()
+    torch.testing.assert_close(s[0], torch.sum(x.double() * y.double()).float(),
+                               rtol=1e-5, atol=1e-4)
