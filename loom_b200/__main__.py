@@ -5,12 +5,14 @@
                                 [--module M ...] [--entry E ...]
                                 [--enable-opt FLAG ...] [--no-multi-gpu]
     python -m loom_b200 compile FILE --entry E --target cuda --out OUT
+                                [--input-kind auto|python|front-ir|tensor-ir]
                                 [--enable-opt FLAG ...]
 
 Entries are read from ``*.tensor_ir.json`` files (the TensorIR the reference
-front end dumps with ``--emit tensor-ir``) and from Python modules written in
-the reference's entry language (``loom.entry`` functions, lowered by
-``loom_b200.frontend``); ``--cuda-arch`` is accepted for compatibility and
+front end dumps with ``--emit tensor-ir``), from ``*.front_ir.json`` files
+(FrontIR, as any Loom frontend writes it) and from Python modules written in
+the reference's entry language (``loom.entry`` functions); the last two are
+lowered by ``loom_b200.frontend``; ``--cuda-arch`` is accepted for compatibility and
 must name sm_100a.
 """
 
@@ -20,6 +22,7 @@ import argparse
 import sys
 
 from . import artifact
+from .frontend import FrontendError
 from .tensor_ir import TensorIRError
 
 
@@ -59,6 +62,8 @@ def main(argv=None) -> int:
     cp.add_argument("file")
     cp.add_argument("--entry", required=True)
     cp.add_argument("--emit", default="all")
+    cp.add_argument("--input-kind", default="auto",
+                    choices=["auto", "python", "front-ir", "tensor-ir"])
     common(cp)
 
     ns = ap.parse_args(argv)
@@ -69,8 +74,9 @@ def main(argv=None) -> int:
         if ns.cmd == "package":
             res = artifact.generate_package(ns.project, ns.out, _options(ns), ns.module, ns.entry)
         else:
-            res = artifact.compile_entry(ns.file, ns.entry, ns.out, _options(ns))
-    except (TensorIRError, artifact.BuildError) as exc:
+            res = artifact.compile_entry(ns.file, ns.entry, ns.out, _options(ns),
+                                         input_kind=ns.input_kind)
+    except (TensorIRError, FrontendError, artifact.BuildError) as exc:
         print(f"error: {exc}", file=sys.stderr)
         return 1
     print(res.artifact_path)

@@ -87,7 +87,7 @@ class EntryBundle:
 
 def module_name_of_file(path: str) -> str:
     base = os.path.basename(path)
-    for suffix in (".tensor_ir.json", ".json", ".py", ".ml", ".cpp"):
+    for suffix in (".tensor_ir.json", ".front_ir.json", ".json", ".py", ".ml", ".cpp"):
         if base.endswith(suffix):
             base = base[: -len(suffix)]
             break
@@ -108,29 +108,51 @@ def _defines_entries(path: str) -> bool:
     return "loom.entry" in text or "@entry" in text
 
 
-def load_source_file(path: str, enabled: Sequence[str] = ()) -> List[Program]:
+def load_front_ir_file(path: str, enabled: Sequence[str] = ()) -> List[Program]:
+    """A ``*.front_ir.json`` file: one FrontIR entry or a list, as any Loom
+    frontend writes it (``loomc compile --input-kind front-ir``,
+    ``src/loom_cli/main.ml:219-226``), lowered through normalize and
+    tensorize here."""
+    from .frontend import program_from_front_ir
+    with open(path, "r", encoding="utf-8") as fh:
+        obj = json.load(fh)
+    return [program_from_front_ir(e, enabled) for e in (obj if isinstance(obj, list) else [obj])]
+
+
+def load_source_file(path: str, enabled: Sequence[str] = (), kind: str = "auto") -> List[Program]:
     """Programs of one source: a ``*.tensor_ir.json`` (one program or a list,
-    taken as given) or a Python module of ``@loom.entry`` functions (through
-    the front end, with the TensorIR passes `enabled` switches on)."""
-    if path.endswith(".py"):
+    taken as given), a ``*.front_ir.json`` (FrontIR entries), or a Python
+    module of ``@loom.entry`` functions (through the front end); the last two
+    with the TensorIR passes `enabled` switches on.  `kind` ("python",
+    "front-ir", "tensor-ir") overrides the choice by file name."""
+    if kind == "auto":
+        kind = ("python" if path.endswith(".py") else
+                "front-ir" if path.endswith(".front_ir.json") else "tensor-ir")
+    if kind == "python":
         from .frontend import python_programs
         return python_programs(path, enabled)
-    return load_entries_file(path)
+    if kind == "front-ir":
+        return load_front_ir_file(path, enabled)
+    if kind == "tensor-ir":
+        return load_entries_file(path)
+    raise TensorIRError(f"unknown input kind {kind!r} (expected python, front-ir or tensor-ir)")
 
 
 def discover_entries(project_root: str, module_filters: Sequence[str] = (),
                      entry_filters: Sequence[str] = (), enabled: Sequence[str] = ()
                      ) -> List[EntryBundle]:
     """Collect entries of a project (cuda_backend.ml:158-178, 307-326): every
-    ``*.tensor_ir.json`` and every Python module with ``@loom.entry``
-    functions below the root, skipping build and hidden dirs, in path order."""
+    ``*.tensor_ir.json``, every ``*.front_ir.json`` and every Python module
+    with ``@loom.entry`` functions below the root, skipping build and hidden
+    dirs, in path order."""
     skip = {"_build", "build", ".venv", ".git", ".hg", ".svn", "node_modules", "__pycache__"}
     found: List[str] = []
     for dirpath, dirnames, filenames in os.walk(project_root):
         dirnames[:] = sorted(d for d in dirnames if d not in skip and not d.startswith("."))
         for name in sorted(filenames):
             path = os.path.join(dirpath, name)
-            if name.endswith(".tensor_ir.json") or (name.endswith(".py") and _defines_entries(path)):
+            if (name.endswith(".tensor_ir.json") or name.endswith(".front_ir.json")
+                    or (name.endswith(".py") and _defines_entries(path))):
                 found.append(path)
     mfilt = [m.lower() for m in module_filters]
     efilt = [e.lower() for e in entry_filters]
@@ -372,11 +394,12 @@ def generate_package(project_root: str, out_dir: str, opts: Optional[Options] = 
 
 
 def compile_entry(source_file: str, entry_name: str, out_dir: str,
-                  opts: Optional[Options] = None, build: bool = True) -> PackageResult:
+                  opts: Optional[Options] = None, build: bool = True,
+                  input_kind: str = "auto") -> PackageResult:
     """``loomc compile <file> --entry e --target cuda`` (cuda_backend.ml:2675-2731)."""
     opts = opts or Options()
     module = module_name_of_file(source_file)
-    progs = [p for p in load_source_file(source_file, opts.enabled)
+    progs = [p for p in load_source_file(source_file, opts.enabled, input_kind)
              if p.entry_name == entry_name]
     if not progs:
         raise TensorIRError(f"entry {entry_name!r} not found in {source_file}")

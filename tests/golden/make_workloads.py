@@ -1,0 +1,63 @@
+"""Regenerate tests/golden/sources/workloads/ from the reference.
+
+The reference's benchmark harness runs 33 supported kernels
+(``experiments/source/data/common/workloads.json``), each a Python entry
+under ``experiments/source/python/``.  For each one this script records:
+
+* ``<name>.front_ir.json``: the FrontIR that the reference's own Python
+  frontend (``src/frontends/python/loom_frontend_python.py front-ir-json``)
+  prints for it -- the input of the B200 project built from this folder;
+* in ``workloads.json``: the entry name, the harness's scalar arguments and
+  tensor inputs, the result kind, and whether this repository's front end
+  printed the same FrontIR from the same source when the fixture was made.
+
+Nothing at test time reads the reference.  Run in a checkout that has it:
+
+    python tests/golden/make_workloads.py /path/to/reference
+"""
+
+import json
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+OUT = os.path.join(HERE, "sources", "workloads")
+
+
+def main(ref: str) -> None:
+    sys.path.insert(0, ROOT)
+    from loom_b200.frontend import front_ir
+
+    frontend = os.path.join(ref, "src", "frontends", "python", "loom_frontend_python.py")
+    spec = json.load(open(os.path.join(ref, "experiments", "source", "data", "common",
+                                       "workloads.json")))
+    os.makedirs(OUT, exist_ok=True)
+    table = []
+    for w in spec["supported_kernels"]:
+        src = os.path.join(ref, "experiments", "source", "python", w["name"] + ".py")
+        proc = subprocess.run([sys.executable, frontend, "front-ir-json", src, "--entry",
+                               w["entry"]], capture_output=True, text=True, check=True)
+        theirs = json.loads(proc.stdout)
+        with open(src, encoding="utf-8") as fh:
+            ours = front_ir(fh.read(), w["entry"])
+        with open(os.path.join(OUT, w["name"] + ".front_ir.json"), "w") as fh:
+            json.dump(theirs, fh, indent=1, sort_keys=True)
+            fh.write("\n")
+        table.append({"name": w["name"], "entry": w["entry"],
+                      "scalar_args": w["scalar_args"], "tensor_inputs": w["tensor_inputs"],
+                      "result_kind": w["result_kind"],
+                      "front_ir_matches_this_front_end": ours == theirs})
+    with open(os.path.join(OUT, "workloads.json"), "w") as fh:
+        json.dump(table, fh, indent=1)
+        fh.write("\n")
+    with open(os.path.join(OUT, "loom-package.json"), "w") as fh:
+        json.dump({"name": "workloads"}, fh)
+        fh.write("\n")
+    same = sum(t["front_ir_matches_this_front_end"] for t in table)
+    print(f"{len(table)} workloads written to {OUT}; this front end matched {same}")
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")

@@ -1,0 +1,135 @@
+"""The reference harness's 33 supported kernels
+(experiments/source/data/common/workloads.json) through this backend.
+
+The fixtures under tests/golden/sources/workloads/ hold the FrontIR that the
+reference's own Python frontend printed for each kernel's source
+(tests/golden/make_workloads.py); this repository's front end printed the
+same FrontIR for all of them when the fixtures were made.  Here that FrontIR
+is lowered (normalize, tensorize), packaged for sm_100a and run:
+
+* CPU: every kernel lowers to valid TensorIR, the package finds all 33
+  entries, and the oracle compiles them;
+* GPU: every kernel against the oracle on the harness's input distribution
+  (N(0,1) tensors, the harness's scalar arguments), built twice: with the
+  default flags, and with the reference's fusion passes and body-rendering
+  flags (loom_b200.build.FUSION_FLAGS + RENDER_FLAGS).  Maps bit-exact (NaN
+  only has to be NaN); sums within 1e-6 * max(1, log2 n) * max(|ref|,
+  sqrt(sum v_i^2)), with v_i the per-element values from a companion map of
+  the reduced body.
+"""
+
+import copy
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+
+from loom_b200 import tensor_ir as TI
+from loom_b200.artifact import discover_entries, load_front_ir_file
+from loom_b200.build import FUSION_FLAGS, RENDER_FLAGS
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+WL_DIR = os.path.join(HERE, "golden", "sources", "workloads")
+TABLE = json.load(open(os.path.join(WL_DIR, "workloads.json")))
+FLAGGED = tuple(FUSION_FLAGS) + tuple(RENDER_FLAGS)
+
+
+def _programs(enabled=()):
+    progs = {}
+    for w in TABLE:
+        for p in load_front_ir_file(os.path.join(WL_DIR, w["name"] + ".front_ir.json"), enabled):
+            progs[w["name"]] = p
+    return progs
+
+
+def values_program(prog: TI.Program) -> TI.Program:
+    """The per-element values a reduction folds, as a map program."""
+    red = prog.node(prog.result.id)
+    assert isinstance(red, TI.Reduce1D)
+    nodes = [copy.deepcopy(n) for n in prog.nodes if n.id != red.id]
+    if isinstance(red.source, TI.PlainInput):
+        result = red.source.input
+        if isinstance(result, TI.ParamRef):      # a plain sum over a parameter
+            nodes.append(TI.Elementwise1D(red.id, (TI.InputBinding("v", result),), (),
+                                          TI.SVar("v")))
+            result = TI.NodeRef(red.id)
+    else:
+        src = red.source
+        nodes.append(TI.Elementwise1D(red.id, src.inputs, src.scalar_params, src.body))
+        result = TI.NodeRef(red.id)
+    return TI.Program(prog.entry_name + "__values", prog.params, "tensor", result, nodes)
+
+
+def test_fixtures_cover_the_harness_kernels():
+    assert len(TABLE) == 33
+    assert all(w["front_ir_matches_this_front_end"] for w in TABLE)
+
+
+@pytest.mark.parametrize("enabled", [(), FLAGGED], ids=["default", "flags"])
+def test_workloads_lower_and_package(enabled):
+    progs = _programs(enabled)
+    assert len(progs) == 33
+    for name, prog in progs.items():
+        TI.validate(prog)
+        w = next(t for t in TABLE if t["name"] == name)
+        assert prog.result_kind == w["result_kind"]
+        assert sorted(p.name for p in prog.tensor_params) == sorted(w["tensor_inputs"])
+    assert len(discover_entries(WL_DIR, enabled=enabled)) == 33
+
+
+def test_oracle_compiles_workloads_and_their_values():
+    from oracle.loom_oracle import Oracle
+    progs = _programs()
+    objs = [TI.program_to_json(p) for p in progs.values()]
+    objs += [TI.program_to_json(values_program(p)) for p in progs.values()
+             if p.result_kind == "scalar"]
+    Oracle(objs, name="workloads_cpu_check")
+
+
+def _inputs(w, n, seed):
+    rng = np.random.default_rng(seed)
+    inp = {t: rng.standard_normal(n).astype(np.float32) for t in w["tensor_inputs"]}
+    inp.update({k: float(v) for k, v in w["scalar_args"].items()})
+    return inp
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("variant", ["default", "flags"])
+def test_workloads_match_oracle(variant):
+    import torch
+
+    from loom_b200.build import build_project
+    from loom_b200.loader import Package
+    from oracle.loom_oracle import Oracle
+    from test_gpu_parity import assert_bits, to_device
+
+    enabled = () if variant == "default" else FLAGGED
+    name = "workloads" if variant == "default" else "workloads_flags"
+    progs = _programs(enabled)
+    pkg = Package(build_project(WL_DIR, enabled=enabled, name=name))
+    objs = [TI.program_to_json(p) for p in progs.values()]
+    objs += [TI.program_to_json(values_program(p)) for p in progs.values()
+             if p.result_kind == "scalar"]
+    oracle = Oracle(objs, name=name, enabled=enabled)
+    for n, offset in ((4099, 1), ((1 << 20) + 3, 0)):
+        for w in TABLE:
+            prog = progs[w["name"]]
+            entry = prog.entry_name
+            inp = _inputs(w, n, seed=n + len(w["name"]))
+            ref = oracle.run(entry, inp)
+            dev = {k: (to_device(v, offset) if isinstance(v, np.ndarray) else v)
+                   for k, v in inp.items()}
+            out = to_device(np.zeros(n, np.float32), offset) if prog.result_kind == "tensor" \
+                else None
+            got = pkg[entry](out=out, **dev)
+            torch.cuda.synchronize()
+            got = got.cpu().numpy()
+            if prog.result_kind == "tensor":
+                assert_bits(got, ref)
+                continue
+            vals = oracle.run(entry + "__values", inp).astype(np.float64)
+            scale = math.sqrt(float(np.sum(vals * vals)))
+            tol = 1e-6 * max(1.0, math.log2(n)) * max(abs(ref), scale)
+            assert abs(float(got[0]) - ref) <= tol, (variant, w["name"], n, float(got[0]), ref)
