@@ -13,7 +13,9 @@ is lowered (normalize, tensorize), packaged for sm_100a and run:
   (N(0,1) tensors, the harness's scalar arguments), built twice: with the
   default flags, and with the reference's fusion passes and body-rendering
   flags (loom_b200.build.FUSION_FLAGS + RENDER_FLAGS).  Maps bit-exact (NaN
-  only has to be NaN); sums within 1e-6 * max(1, log2 n) * max(|ref|,
+  only has to be NaN), except bodies rendered with __fdividef, which are
+  within 2 ulp of the oracle's exact division and are compared at rtol 1e-6;
+  sums within 1e-6 * max(1, log2 n) * max(|ref|,
   sqrt(sum v_i^2)), with v_i the per-element values from a companion map of
   the reduced body.
 """
@@ -22,6 +24,7 @@ import copy
 import json
 import math
 import os
+import re
 
 import numpy as np
 import pytest
@@ -108,11 +111,18 @@ def test_workloads_match_oracle(variant):
     enabled = () if variant == "default" else FLAGGED
     name = "workloads" if variant == "default" else "workloads_flags"
     progs = _programs(enabled)
-    pkg = Package(build_project(WL_DIR, enabled=enabled, name=name))
+    pkg_dir = build_project(WL_DIR, enabled=enabled, name=name)
+    pkg = Package(pkg_dir)
     objs = [TI.program_to_json(p) for p in progs.values()]
     objs += [TI.program_to_json(values_program(p)) for p in progs.values()
              if p.result_kind == "scalar"]
     oracle = Oracle(objs, name=name, enabled=enabled)
+    # map bodies rendered with __fdividef (the ratio-book bodies under
+    # cuda-pointwise-selected-tail-plan): CUDA's fast division is within 2 ulp
+    # of IEEE division for these operands, the oracle divides exactly
+    src = open(os.path.join(pkg_dir, "src-gen", name + ".cu")).read()
+    fast = {m.group(1) for m in re.finditer(r"struct LoomBody_(\w+) \{(.*?)\n\};", src, re.S)
+            if "__fdividef" in m.group(2)}
     for n, offset in ((4099, 1), ((1 << 20) + 3, 0)):
         for w in TABLE:
             prog = progs[w["name"]]
@@ -127,7 +137,10 @@ def test_workloads_match_oracle(variant):
             torch.cuda.synchronize()
             got = got.cpu().numpy()
             if prog.result_kind == "tensor":
-                assert_bits(got, ref)
+                if pkg[entry].symbol in fast:
+                    np.testing.assert_allclose(got, ref, rtol=1e-6, atol=0)
+                else:
+                    assert_bits(got, ref)
                 continue
             vals = oracle.run(entry + "__values", inp).astype(np.float64)
             scale = math.sqrt(float(np.sum(vals * vals)))
