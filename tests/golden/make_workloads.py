@@ -9,7 +9,11 @@ under ``experiments/source/python/``.  For each one this script records:
   prints for it -- the input of the B200 project built from this folder;
 * in ``workloads.json``: the entry name, the harness's scalar arguments and
   tensor inputs, the result kind, and whether this repository's front end
-  printed the same FrontIR from the same source when the fixture was made.
+  printed the same FrontIR from the same source when the fixture was made;
+* ``../workload_limitations.json`` and ``../sources/workload_limitations/``:
+  the harness's unsupported capability cases -- the reference frontend's
+  error, or (where only loomc's later lowering rejects a case) its FrontIR,
+  next to this front end's verdict.
 
 Nothing at test time reads the reference.  Run in a checkout that has it:
 
@@ -57,6 +61,50 @@ def main(ref: str) -> None:
         fh.write("\n")
     same = sum(t["front_ir_matches_this_front_end"] for t in table)
     print(f"{len(table)} workloads written to {OUT}; this front end matched {same}")
+
+    # The harness's capability cases that the reference does not support
+    # (experiments/source/python/limitations/*.py, entry "bad"): the
+    # reference frontend's verdict, and this front end's, for each.
+    from loom_b200.frontend import FrontendError, program_from_front_ir
+    lim_dir = os.path.join(HERE, "sources", "workload_limitations")
+    os.makedirs(lim_dir, exist_ok=True)
+    limitations = {}
+    src_dir = os.path.join(ref, "experiments", "source", "python", "limitations")
+    for name in sorted(os.listdir(src_dir)):
+        if not name.endswith(".py"):
+            continue
+        path = os.path.join(src_dir, name)
+        proc = subprocess.run([sys.executable, frontend, "front-ir-json", path, "--entry", "bad"],
+                              capture_output=True, text=True)
+        with open(path, encoding="utf-8") as fh:
+            text = fh.read()
+        try:
+            ours_front = front_ir(text, "bad", path)
+            ours_error = None
+        except FrontendError as exc:
+            ours_front, ours_error = None, "Python frontend error: " + str(exc)
+        rec = {"reference_frontend_returncode": proc.returncode}
+        if proc.returncode == 0:
+            # accepted by the frontend, rejected later by loomc's lowering
+            theirs = json.loads(proc.stdout)
+            stem = os.path.splitext(name)[0]
+            with open(os.path.join(lim_dir, stem + ".front_ir.json"), "w") as fh:
+                json.dump(theirs, fh, indent=1, sort_keys=True)
+                fh.write("\n")
+            rec["front_ir_matches_this_front_end"] = ours_front == theirs
+            try:
+                program_from_front_ir(theirs)
+                rec["this_lowering_rejects"] = False
+            except FrontendError:
+                rec["this_lowering_rejects"] = True
+        else:
+            rec["reference_error"] = proc.stderr.strip().splitlines()[-1]
+            rec["this_front_end_error"] = ours_error
+        limitations[os.path.splitext(name)[0]] = rec
+    with open(os.path.join(HERE, "workload_limitations.json"), "w") as fh:
+        json.dump(limitations, fh, indent=1, sort_keys=True)
+        fh.write("\n")
+    print(f"{len(limitations)} limitation cases recorded")
 
 
 if __name__ == "__main__":

@@ -146,3 +146,24 @@ def test_workloads_match_oracle(variant):
             scale = math.sqrt(float(np.sum(vals * vals)))
             tol = 1e-6 * max(1.0, math.log2(n)) * max(abs(ref), scale)
             assert abs(float(got[0]) - ref) <= tol, (variant, w["name"], n, float(got[0]), ref)
+
+
+LIMITATIONS = json.load(open(os.path.join(HERE, "golden", "workload_limitations.json")))
+
+
+def test_unsupported_capability_cases_are_rejected():
+    # the harness's unsupported cases (experiments/source/python/limitations):
+    # where the reference frontend rejects one, this front end gave the same
+    # message when the fixtures were made; where only loomc's later lowering
+    # rejects one, its FrontIR is committed and this lowering must reject it
+    from loom_b200.frontend import FrontendError, program_from_front_ir
+    assert len(LIMITATIONS) == 6
+    lim_dir = os.path.join(HERE, "golden", "sources", "workload_limitations")
+    for name, rec in LIMITATIONS.items():
+        if rec["reference_frontend_returncode"] != 0:
+            assert rec["this_front_end_error"] == rec["reference_error"], name
+            continue
+        assert rec["front_ir_matches_this_front_end"], name
+        front = json.load(open(os.path.join(lim_dir, name + ".front_ir.json")))
+        with pytest.raises(FrontendError):
+            program_from_front_ir(front)
