@@ -892,6 +892,49 @@ def run_config_sweep(args) -> None:
           "peak_source": peak_src, "points": points})
 
 
+def run_workload_sweep(args) -> None:
+    """The reference harness's 33 supported kernels (packaged from the
+    FrontIR fixtures in tests/golden/sources/workloads) at N = 2^log2 for
+    each --sweep size (1 GPU): median device time per call (bound calls,
+    CUDA events, 20 calls after 3 warm-up, a write-then-read 512 MiB L2
+    flush before each), inputs N(0,1) and the harness's scalar arguments.
+    GB/s = 4 bytes x (tensor inputs + 1 for a tensor result) x N / time.
+    Prints one JSON line."""
+    import torch
+    from loom_b200.build import BUILT_DIR
+    from loom_b200.loader import Package
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    table_path = os.path.join(ROOT, "tests", "golden", "sources", "workloads", "workloads.json")
+    with open(table_path) as fh:
+        table = json.load(fh)
+    pkg = Package(os.path.join(BUILT_DIR, "workloads"))
+    peak, peak_src = read_peak()
+    stream = torch.cuda.current_stream()
+    flush = (torch.empty(128 << 20, dtype=torch.float32, device="cuda"),
+             torch.ones(128 << 20, dtype=torch.float32, device="cuda"))
+    gen = torch.Generator(device="cuda")
+    points = []
+    for log2n in args.sweep:
+        n = 1 << log2n
+        for k, w in enumerate(table):
+            gen.manual_seed(20260417 + 104729 * k + log2n)
+            kw = {t: torch.randn(n, device="cuda", generator=gen) for t in w["tensor_inputs"]}
+            kw.update({name: float(v) for name, v in w["scalar_args"].items()})
+            tensor_out = w["result_kind"] == "tensor"
+            out = torch.empty(n if tensor_out else 1, device="cuda")
+            call, _ = pkg[w["entry"]].bind(out=out, stream=stream, **kw)
+            us = _median_us(call, 20, flush, stream)
+            nbytes = 4 * n * (len(w["tensor_inputs"]) + (1 if tensor_out else 0))
+            points.append({"workload": w["name"], "log2n": log2n, "us": round(us, 2),
+                           "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+                           "frac": round(nbytes / (us * 1e-6) / 1e9 / peak, 4),
+                           "bytes_per_call": nbytes})
+            del kw, out, call
+        torch.cuda.empty_cache()
+    emit({"mode": "workload_sweep", "metric": METRIC, "unit": "GB/s", "peak": peak,
+          "peak_source": peak_src, "points": points})
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -914,12 +957,17 @@ def main():
     ap.add_argument("--sweep", type=int, nargs="*", default=[10, 14, 18, 22, 26, 30, 32])
     ap.add_argument("--config-sweep", action="store_true",
                     help="time each single-entry configuration at its own N instead of the step")
+    ap.add_argument("--workload-sweep", action="store_true",
+                    help="time the reference harness's 33 kernels at the --sweep sizes")
     args = ap.parse_args()
     protect_stdout()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.config_sweep:
         run_config_sweep(args)
+        return
+    if args.workload_sweep:
+        run_workload_sweep(args)
         return
     if args.pipeline_sweep:
         run_pipeline_sweep(args)
