@@ -246,9 +246,11 @@ def launches_per_call(entry: str, world: int, n: int, peer: bool = True) -> int:
     """Kernels of this library one call launches on n elements per GPU: one
     for a map; for a reduction one when its grid is a single CTA or one
     cluster (at most 8 tiles of 256 threads x 4 float4 for one input, x 2
-    float4 for more), else the reduction kernel and its finalize; across
-    GPUs plus the exchange kernel (peer memory) or, with NCCL, the rank fold
-    for sums (NCCL's own kernels are not counted)."""
+    float4 for more), else the reduction kernel and its finalize.  Across
+    GPUs through peer memory the exchange runs inside the finalize CTA, or
+    as its own kernel after a one-CTA or one-cluster grid, so a reduction is
+    always two kernels; through NCCL the sums add the rank fold (NCCL's own
+    kernels are not counted)."""
     if entry in MAP_ENTRIES:
         return 1
     per_tile = 256 * 4 * (4 if len(TENSORS[entry]) == 1 else 2)
@@ -256,7 +258,7 @@ def launches_per_call(entry: str, world: int, n: int, peer: bool = True) -> int:
     if world == 1:
         return local
     if peer:
-        return local + 1
+        return 2
     return local + (1 if entry != "max_value" else 0)
 
 

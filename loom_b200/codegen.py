@@ -343,6 +343,8 @@ def _render_multi(plan: EntryPlan, async_return: bool) -> List[str]:
                  "return LOOM_STATUS_WORKSPACE_TOO_SMALL;")
     L.append("  }")
     L.append("  loomb::DeviceGuard loom_guard;")
+    if plan.kind != "map":
+        L.append("  const bool loom_peer = loomb::all_peer_exchange(ndev, comms);")
     L.append("  for (int loom_d = 0; loom_d < ndev; ++loom_d) {")
     L.append("    loomb::Comm* loom_c = static_cast<loomb::Comm*>(comms[loom_d]);")
     L.append("    if (cudaSetDevice(loom_c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")
@@ -360,13 +362,20 @@ def _render_multi(plan: EntryPlan, async_return: bool) -> List[str]:
     else:
         op = _op(plan)
         L += ["  " + line for line in _body_setup(plan, lambda name: f"{name}[loom_d]")]
-        L.append(f"    const int loom_status = loomb::dist_local<{op}>(loom_in, shard_n[loom_d], loom_body, "
+        L.append("    // peer memory: reduce and exchange on each device in turn (each exchange")
+        L.append("    // waits for the devices launched after it); NCCL: the local phase only")
+        L.append(f"    const int loom_status = loom_peer")
+        L.append(f"        ? loomb::dist_local_exchange<{op}>(loom_in, shard_n[loom_d], loom_body, "
+                 "workspace[loom_d], out[loom_d], loom_c, nullptr)")
+        L.append(f"        : loomb::dist_local<{op}>(loom_in, shard_n[loom_d], loom_body, "
                  "workspace[loom_d], nullptr);")
         L.append("    if (loom_status != LOOM_STATUS_OK) return loom_status;")
         L.append("  }")
-        L.append(f"  const int loom_exchange = loomb::multi_exchange<{op}>(ndev, comms, workspace, "
-                 "shard_n, out);")
-        L.append("  if (loom_exchange != LOOM_STATUS_OK) return loom_exchange;")
+        L.append("  if (!loom_peer) {")
+        L.append(f"    const int loom_exchange = loomb::multi_nccl_exchange<{op}>(ndev, comms, "
+                 "workspace, shard_n, out);")
+        L.append("    if (loom_exchange != LOOM_STATUS_OK) return loom_exchange;")
+        L.append("  }")
         L.append("  if (host_result != nullptr) {")
         L.append("    loomb::Comm* loom_c0 = static_cast<loomb::Comm*>(comms[0]);")
         L.append("    if (cudaSetDevice(loom_c0->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;")

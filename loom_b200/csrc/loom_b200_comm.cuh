@@ -445,67 +445,102 @@ __device__ __forceinline__ float bits_acc<float>(unsigned long long b) {
   return __uint_as_float((unsigned int)b);
 }
 
-// One thread: take this rank's value (written by the local phase), store it
-// into slot [epoch parity][rank] of every rank's exchange buffer (value,
-// then the epoch with release semantics), then read the nranks values of
-// this epoch from the own buffer (acquire on the epoch) and fold them in
-// rank order into out[0].  The epoch is this rank's own exchange count, kept
-// in device memory, so the kernel also works when replayed from a graph.
-// A wait for a peer's value gives up after the communicator's timeout (30 s
-// unless set), records status 1 in the rank's own exchange buffer and
-// leaves NaN in out[0].  As a backstop that does not depend on the clock, it
-// also gives up after timeout / 16 polls: every poll is an uncached load of
-// far more than 16 ns.
+// What an exchange needs, passed by value to the kernels that do one.
+struct PeerArgs {
+  PeerTable peers;
+  int nranks;
+  int rank;
+  unsigned char* own;              // this rank's exchange buffer
+  float* out;                      // the global result (fp32)
+  unsigned long long timeout_ns;
+};
+
+inline PeerArgs peer_args(const Comm* c, float* out) {
+  PeerArgs a;
+  a.peers = c->peers;
+  a.nranks = c->nranks;
+  a.rank = c->rank;
+  a.own = c->xbuf;
+  a.out = out;
+  a.timeout_ns = c->timeout_ns;
+  return a;
+}
+
+// One thread: store this rank's value into slot [epoch parity][rank] of
+// every rank's exchange buffer (value, then the epoch with release
+// semantics), then read the nranks values of this epoch from the own buffer
+// (acquire on the epoch) and fold them in rank order into out[0].  The epoch
+// is this rank's own exchange count, kept in device memory, so it also works
+// when replayed from a graph.  A wait for a peer's value gives up after the
+// communicator's timeout (30 s unless set), records status 1 in the rank's
+// own exchange buffer and leaves NaN in out[0].  As a backstop that does not
+// depend on the clock, it also gives up after timeout / 16 polls: every poll
+// is an uncached load of far more than 16 ns.
 template <class Op>
-__global__ void peer_exchange_kernel(const typename Op::Acc* __restrict__ local,
-                                     const PeerTable peers, const int nranks, const int rank,
-                                     unsigned char* __restrict__ own, float* __restrict__ out,
-                                     const unsigned long long timeout_ns) {
+__device__ __forceinline__ void exchange_and_fold(const typename Op::Acc local,
+                                                  const PeerArgs& a) {
   using Acc = typename Op::Acc;
-  wait_for_prerequisite_grid();
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  unsigned long long* counter = reinterpret_cast<unsigned long long*>(own);
-  unsigned int* status = reinterpret_cast<unsigned int*>(own + 8);
+  unsigned long long* counter = reinterpret_cast<unsigned long long*>(a.own);
+  unsigned int* status = reinterpret_cast<unsigned int*>(a.own + 8);
   const unsigned long long epoch = *counter + 1;
   *counter = epoch;
   const int set = (int)(epoch & 1ull) * kMaxRanks;
-  const unsigned long long bits = acc_bits(*local);
-  for (int r = 0; r < nranks; ++r) {
+  const unsigned long long bits = acc_bits(local);
+  for (int r = 0; r < a.nranks; ++r) {
     ExchangeSlot* s =
-        reinterpret_cast<ExchangeSlot*>(peers.buf[r] + kExchangeSlotsOffset) + set + rank;
+        reinterpret_cast<ExchangeSlot*>(a.peers.buf[r] + kExchangeSlotsOffset) + set + a.rank;
     st_relaxed_sys(&s->bits, bits);
     st_release_sys(&s->epoch, epoch);
   }
-  ExchangeSlot* mine = reinterpret_cast<ExchangeSlot*>(own + kExchangeSlotsOffset) + set;
+  ExchangeSlot* mine = reinterpret_cast<ExchangeSlot*>(a.own + kExchangeSlotsOffset) + set;
   Acc total = Op::init();
   const unsigned long long t0 = global_ns();
-  const unsigned long long max_polls = timeout_ns / 16 + 1;
+  const unsigned long long max_polls = a.timeout_ns / 16 + 1;
   unsigned long long polls = 0;
-  for (int r = 0; r < nranks; ++r) {
+  for (int r = 0; r < a.nranks; ++r) {
     while (ld_acquire_sys(&mine[r].epoch) != epoch) {
-      if (++polls > max_polls || global_ns() - t0 > timeout_ns) {
+      if (++polls > max_polls || global_ns() - t0 > a.timeout_ns) {
         atomicExch(status, 1u);
-        out[0] = __int_as_float(0x7fffffff);  // NaN: no result
+        a.out[0] = __int_as_float(0x7fffffff);  // NaN: no result
         return;
       }
       __nanosleep(32);
     }
     total = Op::combine(total, bits_acc<Acc>(ld_relaxed_sys(&mine[r].bits)));
   }
-  out[0] = Op::to_float(total);
+  a.out[0] = Op::to_float(total);
 }
 
-// The exchange kernel as a programmatic dependent of the local phase (its
-// griddepcontrol.wait holds it until that phase has finished); a plain
-// launch where the attribute is refused.
+// The exchange after a first stage that left this rank's value in `local`
+// (a one-CTA or one-cluster grid).
 template <class Op>
-inline int launch_peer_exchange(void* workspace, int64_t n_local, float* out, Comm* comm,
-                                cudaStream_t stream) {
-  RankSlots<Op> slots(workspace, n_local);
-  const typename Op::Acc* local = slots.local;
+__global__ void peer_exchange_kernel(const typename Op::Acc* __restrict__ local,
+                                     const PeerArgs a) {
+  wait_for_prerequisite_grid();
+  if (threadIdx.x == 0 && blockIdx.x == 0) exchange_and_fold<Op>(*local, a);
+}
+
+// The finalize and the exchange in one kernel: the CTA folds this rank's
+// partials, then its thread 0 exchanges the total with the other ranks over
+// NVLink and folds theirs.
+template <class Op>
+__global__ void __launch_bounds__(kFinalizeThreads)
+finalize_exchange_kernel(const typename Op::Acc* __restrict__ partials, const int count,
+                         const PeerArgs a) {
+  wait_for_prerequisite_grid();
+  allow_dependent_launch();
+  const typename Op::Acc acc = fold_partials<Op>(partials, count);
+  if (threadIdx.x == 0) exchange_and_fold<Op>(acc, a);
+}
+
+// A one-CTA kernel as a programmatic dependent of the kernel before it on
+// the stream (its griddepcontrol.wait holds it until that one has finished);
+// a plain launch where the attribute is refused.
+template <class Kern, class... Args>
+inline int launch_dependent_cta(Kern kernel, int threads, cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
-  cfg.blockDim = dim3(32);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -513,43 +548,62 @@ inline int launch_peer_exchange(void* workspace, int64_t n_local, float* out, Co
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, peer_exchange_kernel<Op>, local, comm->peers, comm->nranks,
-                         comm->rank, comm->xbuf, out, comm->timeout_ns) == cudaSuccess)
-    return LOOM_STATUS_OK;
+  if (cudaLaunchKernelEx(&cfg, kernel, args...) == cudaSuccess) return LOOM_STATUS_OK;
   cudaGetLastError();
-  peer_exchange_kernel<Op><<<1, 32, 0, stream>>>(local, comm->peers, comm->nranks, comm->rank,
-                                                 comm->xbuf, out, comm->timeout_ns);
+  kernel<<<1, threads, 0, stream>>>(args...);
   return launch_status();
+}
+
+// This rank's shard reduced and exchanged through peer memory: the first
+// stage, then either the fused finalize-and-exchange CTA (when the stage
+// left partials) or the exchange kernel alone.  An empty shard exchanges
+// Op's identity.
+template <class Op, class Body>
+inline int dist_local_exchange(const Ptrs<Body::kInputs>& in, int64_t n_local, const Body& body,
+                               void* workspace, float* out, const Comm* comm,
+                               cudaStream_t stream) {
+  RankSlots<Op> slots(workspace, n_local);
+  auto* partials = reinterpret_cast<typename Op::Acc*>(workspace_base(workspace));
+  const PeerArgs a = peer_args(comm, out);
+  if (n_local == 0)
+    return launch_dependent_cta(finalize_exchange_kernel<Op>, kFinalizeThreads, stream,
+                                static_cast<const typename Op::Acc*>(partials), 0, a);
+  unsigned pending = 0;
+  const int st = launch_reduce_stage<Op>(in, n_local, body, partials, partial_capacity(n_local),
+                                         nullptr, slots.local, stream, &pending);
+  if (st != LOOM_STATUS_OK) return st;
+  if (pending == 0)
+    return launch_dependent_cta(peer_exchange_kernel<Op>, 32, stream,
+                                static_cast<const typename Op::Acc*>(slots.local), a);
+  return launch_dependent_cta(finalize_exchange_kernel<Op>, kFinalizeThreads, stream,
+                              static_cast<const typename Op::Acc*>(partials), (int)pending, a);
 }
 
 template <class Op, class Body>
 inline int dist_reduce(const Ptrs<Body::kInputs>& in, int64_t n_local, const Body& body,
                        void* workspace, float* out, Comm* comm, cudaStream_t stream) {
+  if (comm->peer_exchange)
+    return dist_local_exchange<Op>(in, n_local, body, workspace, out, comm, stream);
   int st = dist_local<Op>(in, n_local, body, workspace, stream);
   if (st != LOOM_STATUS_OK) return st;
-  if (comm->peer_exchange) return launch_peer_exchange<Op>(workspace, n_local, out, comm, stream);
   st = dist_collective<Op>(workspace, n_local, out, comm, stream);
   if (st != LOOM_STATUS_OK) return st;
   return dist_finish<Op>(workspace, n_local, out, comm, stream);
 }
 
-// One process, ndev GPUs, after the local phase on every device: the peer
-// exchange on every device (launched one device after another; each waits
-// for the others), or one grouped NCCL collective and the rank fold.
+// Whether every communicator of a one-process group exchanges through peer
+// memory (else the group uses NCCL).
+inline bool all_peer_exchange(int ndev, void* const* comms) {
+  for (int d = 0; d < ndev; ++d)
+    if (!static_cast<Comm*>(comms[d])->peer_exchange) return false;
+  return true;
+}
+
+// One process, ndev GPUs, on the NCCL path, after the local phase on every
+// device: one grouped NCCL collective and the rank fold on every device.
 template <class Op>
-inline int multi_exchange(int ndev, void* const* comms, void* const* workspace,
-                          const int64_t* shard_n, float* const* out) {
-  bool peer = true;
-  for (int d = 0; d < ndev; ++d) peer = peer && static_cast<Comm*>(comms[d])->peer_exchange;
-  if (peer) {
-    for (int d = 0; d < ndev; ++d) {
-      Comm* c = static_cast<Comm*>(comms[d]);
-      if (cudaSetDevice(c->device) != cudaSuccess) return LOOM_STATUS_CUDA_ERROR;
-      const int st = launch_peer_exchange<Op>(workspace[d], shard_n[d], out[d], c, nullptr);
-      if (st != LOOM_STATUS_OK) return st;
-    }
-    return LOOM_STATUS_OK;
-  }
+inline int multi_nccl_exchange(int ndev, void* const* comms, void* const* workspace,
+                               const int64_t* shard_n, float* const* out) {
   if (nccl_group_start() != 0) return LOOM_STATUS_COMM_ERROR;
   int group_status = LOOM_STATUS_OK;
   for (int d = 0; d < ndev && group_status == LOOM_STATUS_OK; ++d) {

@@ -410,20 +410,15 @@ reduce_scalar_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::k
   store_reduction<Op, false>(acc, partials, out, partial_out);
 }
 
-// One CTA folds `count` CTA partials in a fixed order: each thread issues 16
-// independent loads per round (the partials are in L2, so the fold is bound
-// by load latency, not bandwidth) into four interleaved accumulators, then
-// the CTA tree.  Writes the fp32 result to
-// `out` (if non-null) and the full-precision value to `partial_out` (if
-// non-null; the multi-GPU path all-gathers it).
+// One CTA of kFinalizeThreads folds `count` CTA partials in a fixed order:
+// each thread issues 16 independent loads per round (the partials are in L2,
+// so the fold is bound by load latency, not bandwidth) into four interleaved
+// accumulators, then the CTA tree.  The result is valid in thread 0.
 template <class Op>
-__global__ void __launch_bounds__(kFinalizeThreads)
-reduce_finalize_kernel(const typename Op::Acc* __restrict__ partials, const int count,
-                       float* __restrict__ out, typename Op::Acc* __restrict__ partial_out) {
+__device__ __forceinline__ typename Op::Acc fold_partials(
+    const typename Op::Acc* __restrict__ partials, const int count) {
   using Acc = typename Op::Acc;
   constexpr int T = kFinalizeThreads;
-  wait_for_prerequisite_grid();
-  allow_dependent_launch();
   constexpr int kLoads = 16;
   Acc a[4] = {Op::init(), Op::init(), Op::init(), Op::init()};
   int i = threadIdx.x;
@@ -435,8 +430,20 @@ reduce_finalize_kernel(const typename Op::Acc* __restrict__ partials, const int 
     for (int j = 0; j < kLoads; ++j) a[j & 3] = Op::combine(a[j & 3], v[j]);
   }
   for (; i < count; i += T) a[0] = Op::combine(a[0], partials[i]);
-  Acc acc = Op::combine(Op::combine(a[0], a[1]), Op::combine(a[2], a[3]));
-  acc = block_reduce<Op, T>(acc);
+  const Acc acc = Op::combine(Op::combine(a[0], a[1]), Op::combine(a[2], a[3]));
+  return block_reduce<Op, T>(acc);
+}
+
+// The finalize CTA: folds the partials, writes the fp32 result to `out` (if
+// non-null) and the full-precision value to `partial_out` (if non-null; the
+// multi-GPU path exchanges it).
+template <class Op>
+__global__ void __launch_bounds__(kFinalizeThreads)
+reduce_finalize_kernel(const typename Op::Acc* __restrict__ partials, const int count,
+                       float* __restrict__ out, typename Op::Acc* __restrict__ partial_out) {
+  wait_for_prerequisite_grid();
+  allow_dependent_launch();
+  const typename Op::Acc acc = fold_partials<Op>(partials, count);
   if (threadIdx.x == 0) {
     if (out != nullptr) out[0] = Op::to_float(acc);
     if (partial_out != nullptr) partial_out[0] = acc;

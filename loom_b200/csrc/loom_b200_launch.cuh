@@ -207,13 +207,18 @@ inline int launch_map(float* out, const Ptrs<Body::kInputs>& in, int64_t n, cons
   return launch_status();
 }
 
-// Reduces body(in[...][i]) over [0, n) with Op into out[0] (fp32) and/or
-// partial_out[0] (Op::Acc).  `partials` must hold `max_partials` slots
-// (at least 1); the first kernel uses at most that many CTAs.
+// The first stage of a reduction of body(in[...][i]) over [0, n) with Op.
+// `partials` must hold `max_partials` slots (at least 1); the kernel uses at
+// most that many CTAs.  On return *pending is the number of CTA partials left
+// in `partials` for a finalize to fold, or 0 when the stage already wrote
+// the result to out[0] (fp32) and/or partial_out[0] (Op::Acc): a one-CTA
+// grid, or a grid of at most kMaxClusterCtas launched as one cluster.
 template <class Op, class Body>
-inline int launch_reduce(const Ptrs<Body::kInputs>& in, int64_t n, const Body& body,
-                         typename Op::Acc* partials, int64_t max_partials, float* out,
-                         typename Op::Acc* partial_out, cudaStream_t stream) {
+inline int launch_reduce_stage(const Ptrs<Body::kInputs>& in, int64_t n, const Body& body,
+                               typename Op::Acc* partials, int64_t max_partials, float* out,
+                               typename Op::Acc* partial_out, cudaStream_t stream,
+                               unsigned* pending) {
+  *pending = 0;
   if (n <= 0 || max_partials < 1) return LOOM_STATUS_INVALID_ARGUMENT;
   if (!pointers_aligned4(in, nullptr)) return LOOM_STATUS_INVALID_ARGUMENT;
   unsigned grid;
@@ -232,9 +237,23 @@ inline int launch_reduce(const Ptrs<Body::kInputs>& in, int64_t n, const Body& b
     reduce_scalar_kernel<Op, Body><<<grid, kThreads, 0, stream>>>(partials, in, n, body, out,
                                                                   partial_out);
   }
-  int st = launch_status();
-  if (st != LOOM_STATUS_OK || grid == 1) return st;  // one CTA wrote the result itself
-  return launch_finalize<Op>(partials, (int)grid, out, partial_out, stream);
+  const int st = launch_status();
+  if (st == LOOM_STATUS_OK && grid > 1) *pending = grid;  // one CTA wrote the result itself
+  return st;
+}
+
+// Reduces body(in[...][i]) over [0, n) with Op into out[0] (fp32) and/or
+// partial_out[0] (Op::Acc): the first stage, then the finalize CTA where
+// partials are left.
+template <class Op, class Body>
+inline int launch_reduce(const Ptrs<Body::kInputs>& in, int64_t n, const Body& body,
+                         typename Op::Acc* partials, int64_t max_partials, float* out,
+                         typename Op::Acc* partial_out, cudaStream_t stream) {
+  unsigned pending = 0;
+  const int st = launch_reduce_stage<Op>(in, n, body, partials, max_partials, out, partial_out,
+                                         stream, &pending);
+  if (st != LOOM_STATUS_OK || pending == 0) return st;
+  return launch_finalize<Op>(partials, (int)pending, out, partial_out, stream);
 }
 
 // Blocks until the device is idle, mapping the result to a status code (the

@@ -61,7 +61,7 @@ def test_launch_counts():
     assert [bench.launches_per_call(e, 4, n, peer=False) for e in bench.ENTRIES] == \
         [1, 1, 3, 3, 2, 1, 3]
     assert [bench.launches_per_call(e, 4, n, peer=True) for e in bench.ENTRIES] == \
-        [1, 1, 3, 3, 3, 1, 3]
+        [1, 1, 2, 2, 2, 1, 2]
     assert all(bench.launches_per_call(e, 1, 4096) == 1 for e in bench.ENTRIES)
 
 
