@@ -40,10 +40,10 @@ class SConstF32:
     # CUDA renderer prints it with "%.12g", so keep the double here.
     value: float
 
-    def __eq__(self, other):  # OCaml structural equality on floats
-        return isinstance(other, SConstF32) and (
-            self.value == other.value
-            or (math.isnan(self.value) and math.isnan(other.value)))
+    def __eq__(self, other):
+        # OCaml's structural `=` compares floats as IEEE values: -0.0 = 0.0,
+        # and a NaN equals nothing (the reference's pattern guards use it)
+        return isinstance(other, SConstF32) and self.value == other.value
 
     def __hash__(self):
         return hash(("f32", self.value))

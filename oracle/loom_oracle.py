@@ -78,13 +78,23 @@ def cpp_float(value: float) -> str:
     return text + ".0f"
 
 
-def _key(e):
-    """Structural identity of an expression (OCaml '=')."""
-    return json.dumps(e, sort_keys=True)
-
-
 def _eq(a, b) -> bool:
-    return _key(a) == _key(b)
+    """OCaml's structural '=' on two expressions: floats compare as IEEE
+    values (-0.0 = 0.0, NaN equals nothing), everything else by value."""
+    if a["kind"] != b["kind"]:
+        return False
+    k = a["kind"]
+    if k == "f32":
+        return float(a["value"]) == float(b["value"])
+    if k in ("var",):
+        return a["name"] == b["name"]
+    if k == "bool":
+        return bool(a["value"]) == bool(b["value"])
+    if k == "unary":
+        return a["op"] == b["op"] and _eq(a["expr"], b["expr"])
+    if k == "binary":
+        return a["op"] == b["op"] and _eq(a["lhs"], b["lhs"]) and _eq(a["rhs"], b["rhs"])
+    return _eq(a["cond"], b["cond"]) and _eq(a["then"], b["then"]) and _eq(a["else"], b["else"])
 
 
 def _is_zero(e) -> bool:

@@ -166,3 +166,19 @@ def test_node_flag_derivation_restatements_agree():
         assert (mine.tail_tune, mine.predicated_select, mine.fast_divide,
                 mine.eager_select_then) == (ref["tail_tune"], ref["predicated_select"],
                                             ref["fast_divide"], ref["eager_select_then"])
+
+
+def test_literal_equality_is_ieee_as_in_ocaml():
+    # The reference's pattern guards compare expressions with OCaml's
+    # structural `=`, which compares floats as IEEE values: the literal -0.0
+    # equals 0.0 (so `x > 0.0 ? x : -0.0` still reuses the compared value and
+    # becomes fmaxf), and NaN equals nothing (so `x > nan ? x : nan` stays a
+    # ternary).  Both restatements must follow that.
+    neg_zero = T.SSelect(B("cmpgt", V("xi"), C(0.0)), V("xi"), C(-0.0))
+    assert C(-0.0) == C(0.0) and C(float("nan")) != C(float("nan"))
+    assert product_lines(neg_zero) == oracle_lines(neg_zero)
+    assert "fmaxf" in product_lines(neg_zero)[-1]
+    nan = float("nan")
+    with_nan = T.SSelect(B("cmpgt", V("xi"), C(nan)), V("xi"), C(nan))
+    assert product_lines(with_nan) == oracle_lines(with_nan)
+    assert "fmaxf" not in "".join(product_lines(with_nan))
