@@ -12,7 +12,8 @@ reduced per-element values, so the test can size the sum's tolerance.
 Bodies use the operators whose fp32 results are exactly rounded on both the
 GPU and the host (add, sub, mul, div, min, max, neg, sqrt, comparisons and
 select), so every map and max must match the oracle bit for bit.  Constants
-include fractional ones, which the reference renders as double literals.
+include fractional ones, which the reference renders as double literals, and
+-0.0, which its pattern guards treat as equal to 0.0.
 
 Run from the repository root: python tests/golden/sources/random/make_random_programs.py
 """
@@ -31,7 +32,7 @@ from loom_b200.frontend.lower import annotate  # noqa: E402
 
 SEED = 20260417
 N_PROGRAMS = 36
-CONSTS = [0.0, 1.0, -1.0, 2.0, 3.0, 0.5, 0.25, -0.75, 1.5, 0.001, 10.0]
+CONSTS = [0.0, -0.0, 1.0, -1.0, 2.0, 3.0, 0.5, 0.25, -0.75, 1.5, 0.001, 10.0]
 
 
 def fexpr(rng, depth, names):
