@@ -42,13 +42,23 @@ GENCODE = "arch=compute_100a,code=sm_100a"
 HONOURED_FLAGS = {"cuda-async-wrapper-return", "cuda-pointwise-tail-tune",
                   "cuda-pointwise-predicated-select", "cuda-pointwise-selected-tail-plan",
                   "cuda-body-trait-analysis", "shared-body-trait-analysis"}
-# The TensorIR fusion passes and the policy flags that steer them, which the
-# Python front end applies to Python sources (frontend/passes.py); TensorIR
-# files are taken as given, as `loomc` ran its passes before writing them.
+# The LoomLambda scalar passes, the TensorIR passes and the policy flags that
+# steer fusion, which the front end applies to Python and FrontIR sources
+# (frontend/normalize_passes.py, frontend/passes.py); TensorIR files are
+# taken as given, as `loomc` ran its passes before writing them.
 FRONTEND_PASS_FLAGS = {"map-chain-collapse", "elementwise-fusion", "small-producer-clone",
                        "reduce-map-fusion", "shape-use-simplify", "materialization-choice",
                        "reduction-materialization-choice", "reduction-late-fusion-guard",
-                       "branch-aware-fusion-guard", "pointwise-materialization-guard"}
+                       "branch-aware-fusion-guard", "pointwise-materialization-guard",
+                       # normalize_scalar.ml
+                       "scalar-const-fold", "if-simplify", "arith-reassociate", "let-float",
+                       "branch-hoist", "lambda-inline-small", "scalar-cse", "normalized-dce",
+                       "scalar-hoist",
+                       # tensor_passes.ml body rewrites and node CSE
+                       "tensor-canonicalize", "reduction-input-simplify",
+                       "reduction-body-normalize", "reduction-accumulator-shape",
+                       "reduction-reuse-hoist", "branchy-reduction-rescue",
+                       "reduction-body-canonicalize", "reduction-body-cse", "tensor-cse"}
 
 
 class BuildError(RuntimeError):

@@ -27,6 +27,27 @@ SUITE_DIR = os.path.join(BUILT_DIR, "b200_suite")
 FUSION_FLAGS = ["map-chain-collapse", "reduce-map-fusion", "shape-use-simplify"]
 RENDER_FLAGS = ["cuda-pointwise-tail-tune", "cuda-pointwise-predicated-select",
                 "cuda-pointwise-selected-tail-plan", "cuda-body-trait-analysis"]
+# The flag set of the reference harness's tuned CUDA profile, "loom_cuda_fixed"
+# (experiments/source/data/profiles/loom_profiles.json): its scalar and
+# TensorIR passes (restated in loom_b200/frontend/), its fusion, and its
+# rendering flags.
+CUDA_FIXED_FLAGS = [
+    "scalar-const-fold", "if-simplify", "arith-reassociate", "lambda-inline-small", "scalar-cse",
+    "normalized-dce", "tensor-canonicalize", "reduction-input-simplify",
+    "reduction-body-normalize", "reduction-body-canonicalize", "reduction-accumulator-shape",
+    "reduction-reuse-hoist", "reduction-body-cse", "map-chain-collapse", "reduce-map-fusion",
+    "shape-use-simplify", "tensor-cse", "materialization-choice",
+    "reduction-materialization-choice", "reduction-plan-specialize", "reduction-classify",
+    "reduction-tree-plan", "reduction-split-plan", "reduction-small-plan-specialize",
+    "reduction-stage-sizing", "reduction-stage-balance", "reduction-partial-shape-pack",
+    "reduction-class-aware-buckets", "shared-body-trait-analysis", "cuda-body-trait-analysis",
+    "cuda-reduction-instruction-select", "cuda-reduction-tail-tune", "cuda-reduction-norm-plan",
+    "cuda-reduction-dot-plan", "cuda-reduction-weighted-product-plan",
+    "cuda-pointwise-small-shape-plan", "cuda-pointwise-medium-plan",
+    "cuda-pointwise-predicated-select", "cuda-pointwise-selected-tail-plan",
+    "cuda-pointwise-vectorize", "cuda-pointwise-tail-tune", "cuda-reduction-shuffle",
+    "cuda-reduction-medium-tail-plan", "cuda-async-wrapper-return", "cuda-selected-profile",
+    "storage-reuse-pack", "launch-bucket-specialize"]
 
 
 def SUITE_OPTIONS() -> artifact.Options:

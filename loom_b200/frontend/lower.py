@@ -17,6 +17,10 @@ the default (empty) optimisation set:
   definitions of ``src/loom_tensorize/reduction_analysis.ml:1-290``): use
   counts, body metrics and the reduction shape.
 
+With optimisation flags, the reference's LoomLambda scalar passes run after
+normalize (normalize_passes.py) and its TensorIR passes after tensorize
+(passes.py).
+
 The output is the TensorIR the reference hands its CUDA backend for the same
 source, node for node (checked against the reference's golden TensorIR and
 LoomLambda files in tests/test_frontend.py).
@@ -168,11 +172,15 @@ def _norm(e, env):
     raise FrontendError(f"unknown FrontIR node kind {k!r}")
 
 
-def loom_lambda(front: dict) -> dict:
-    """FrontIR entry -> LoomLambda entry (JSON form of loomLambda.ml:74-137)."""
+def loom_lambda(front: dict, enabled=()) -> dict:
+    """FrontIR entry -> LoomLambda entry (JSON form of loomLambda.ml:74-137),
+    after the scalar passes that `enabled` switches on (normalize.ml:195-258;
+    normalize_passes.py)."""
+    from .normalize_passes import apply_normalize_passes
     env = {p["name"]: _Value(_var(p["name"], p["type"])) for p in front["params"]}
+    body = apply_normalize_passes(_norm(front["body"], env), enabled)
     return {"entry": front["entry"], "params": [dict(p) for p in front["params"]],
-            "return_type": front["return_type"], "body": _norm(front["body"], env)}
+            "return_type": front["return_type"], "body": body}
 
 
 # ---------------------------------------------------------------------------
@@ -404,7 +412,11 @@ def annotate(prog: TI.Program, enabled=()) -> TI.Program:
                 n.reduction_shape = "plain"
             else:
                 b = n.source.body
-                n.metrics = body_metrics(u, b)
+                if "reduction-body-canonicalize" in enabled:
+                    from .analysis import adjusted_reduction_body_metrics
+                    n.metrics = adjusted_reduction_body_metrics(n.source.scalar_params, u, b)
+                else:
+                    n.metrics = body_metrics(u, b)
                 has_sel = _count(b, lambda x: isinstance(x, TI.SSelect)) > 0
                 has_div = _count(b, lambda x: isinstance(x, TI.SBinary) and x.op == "div") > 0
                 n.reduction_shape = ("branchy-mapped" if has_sel else "ratio-mapped" if has_div
@@ -447,4 +459,4 @@ def tensor_ir(lam: dict, enabled=()) -> TI.Program:
 
 
 def program_from_front_ir(front: dict, enabled=()) -> TI.Program:
-    return tensor_ir(loom_lambda(front), enabled)
+    return tensor_ir(loom_lambda(front, enabled), enabled)

@@ -19,12 +19,24 @@ each gated by the materialisation policy
 hints that annotation attaches (``materialization_hint``, ``:1-44``).  The
 thresholds are the reference's defaults (``configs/optimizations/current.json``).
 
+and the body rewrites and node CSE (``:6-60``, ``:337-513``), applied before
+and again after fusion (``:554-666``):
+
+* ``tensor-canonicalize`` -- operands of +, *, min, max, == in rank order,
+  compare-and-pick selects turned into min/max;
+* ``reduction-input-simplify`` -- constant folding and algebraic identities;
+* ``reduction-body-normalize`` / ``reduction-accumulator-shape``,
+  ``reduction-reuse-hoist``, ``reduction-body-canonicalize``,
+  ``branchy-reduction-rescue``, ``reduction-body-cse`` -- the same rewrites,
+  and product reordering, on mapped-reduction bodies;
+* ``tensor-cse`` -- nodes with equal keys merged.
+
 The B200 plan inlines every element-wise chain into one kernel whether or
-not these passes ran, so they change the TensorIR (and its dump under
-``entries/``), not the kernels; what they can change is which rendering
-flags apply to a body, since a body fused into a reduction renders with the
-defaults.  The reference's other TensorIR passes (CSE, canonicalisation,
-reduction-body rewrites) are not restated.
+not the fusion passes ran, so those change the TensorIR (and its dump under
+``entries/``), not the kernels, except for which rendering flags apply to a
+body (a body fused into a reduction renders with the defaults).  The body
+rewrites do change the kernels: a reordered sum or a folded constant rounds
+differently, and the oracle, which evaluates the rewritten TensorIR, follows.
 """
 
 from __future__ import annotations
@@ -32,6 +44,7 @@ from __future__ import annotations
 from typing import Dict, List, Sequence, Tuple
 
 from .. import tensor_ir as TI
+from . import analysis as A
 from .lower import _use_counts, body_metrics
 
 # configs/optimizations/current.json (the reference's defaults)
@@ -265,9 +278,165 @@ def shape_use_simplify(prog: TI.Program) -> TI.Program:
     return prog
 
 
+# --- body rewrites and CSE (tensor_passes.ml:6-60, 337-510) ----------------------
+
+def _with_mapped(node: TI.Reduce1D, **changes) -> None:
+    src = node.source
+    node.source = TI.MappedInput(changes.get("inputs", src.inputs),
+                                 changes.get("scalar_params", src.scalar_params),
+                                 changes.get("body", src.body))
+
+
+def _mapped(prog: TI.Program):
+    return [n for n in prog.nodes
+            if isinstance(n, TI.Reduce1D) and isinstance(n.source, TI.MappedInput)]
+
+
+def canonicalize_program(prog: TI.Program) -> TI.Program:
+    """tensor-canonicalize: scalar parameters sorted and unique, bodies in
+    canonical operand order (tensor_passes.ml:6-33)."""
+    for n in prog.nodes:
+        if isinstance(n, TI.Elementwise1D):
+            n.scalar_params = tuple(sorted(set(n.scalar_params)))
+            n.body = A.canonicalize(n.body)
+    for n in _mapped(prog):
+        _with_mapped(n, scalar_params=tuple(sorted(set(n.source.scalar_params))),
+                     body=A.canonicalize(n.source.body))
+    return prog
+
+
+def simplify_program(prog: TI.Program) -> TI.Program:
+    """reduction-input-simplify: every body simplified (tensor_passes.ml:35-60)."""
+    for n in prog.nodes:
+        if isinstance(n, TI.Elementwise1D):
+            n.body = A.simplify(n.body)
+    for n in _mapped(prog):
+        _with_mapped(n, body=A.simplify(n.source.body))
+    return prog
+
+
+def reduction_body_normalize(prog: TI.Program) -> TI.Program:
+    """Mapped reductions: parameters sorted, inputs sorted by name, body
+    canonicalised then simplified (tensor_passes.ml:337-358)."""
+    for n in _mapped(prog):
+        src = n.source
+        _with_mapped(n, scalar_params=tuple(sorted(set(src.scalar_params))),
+                     inputs=tuple(sorted(src.inputs, key=lambda b: b.name)),
+                     body=A.simplify(A.canonicalize(src.body)))
+    return prog
+
+
+def reduction_reuse_hoist(prog: TI.Program) -> TI.Program:
+    """tensor_passes.ml:360-376."""
+    for n in _mapped(prog):
+        _with_mapped(n, body=A.simplify(A.canonicalize(A.simplify(n.source.body))))
+    return prog
+
+
+def reduction_body_canonicalize(prog: TI.Program) -> TI.Program:
+    """Products with data factors before scalar weights (tensor_passes.ml:378-394)."""
+    for n in _mapped(prog):
+        body = A.canonicalize_reduction_body(n.source.scalar_params, n.source.body)
+        _with_mapped(n, body=A.canonicalize(A.simplify(body)))
+    return prog
+
+
+def branchy_reduction_rescue(prog: TI.Program) -> TI.Program:
+    """tensor_passes.ml:396-412."""
+    for n in _mapped(prog):
+        body = A.branchy_weighted_rescue_body(n.source.scalar_params, n.source.body)
+        _with_mapped(n, body=A.canonicalize(A.simplify(body)))
+    return prog
+
+
+def reduction_body_cse(prog: TI.Program) -> TI.Program:
+    """Bodies with at least REDUCTION_BODY_CSE_MIN_OCCURRENCES repeated
+    subexpressions (tensor_passes.ml:414-438)."""
+    for n in _mapped(prog):
+        body = n.source.body
+        if A.repeated_subexpressions(body) >= REDUCTION_BODY_CSE_MIN_OCCURRENCES:
+            _with_mapped(n, body=A.canonicalize(A.simplify(A.reduction_body_cse_expr(body))))
+    return prog
+
+
+def _ref_key(ref: TI.ValueRef) -> str:
+    return "p:" + ref.name if isinstance(ref, TI.ParamRef) else "n:%d" % ref.id
+
+
+def _bindings_key(bindings) -> str:
+    return "|".join(b.name + "=" + _ref_key(b.source) for b in bindings)
+
+
+def _node_key(n: TI.Node) -> str:
+    if isinstance(n, TI.Elementwise1D):
+        return "e:%s:%s:%s:%s" % (n.shape_symbol, _bindings_key(n.inputs),
+                                  ",".join(n.scalar_params), A.scalar_rank(n.body))
+    if isinstance(n.source, TI.PlainInput):
+        src = "p:" + _ref_key(n.source.input)
+    else:
+        src = "m:%s:%s:%s" % (_bindings_key(n.source.inputs), ",".join(n.source.scalar_params),
+                              A.scalar_rank(n.source.body))
+    return "r:%s:%s:%s" % (n.shape_symbol, n.kind, src)
+
+
+def tensor_cse(prog: TI.Program) -> TI.Program:
+    """A node whose key equals an earlier node's is dropped and its uses
+    redirected to that node (tensor_passes.ml:440-513).  The key holds the
+    body's rank, in which a unary's operator does not appear, so two maps of
+    the same input that differ only in a unary operator merge, as there."""
+    redirects: Dict[int, TI.ValueRef] = {}
+    seen: Dict[str, int] = {}
+    remap = lambda r: redirects.get(r.id, r) if isinstance(r, TI.NodeRef) else r
+    keep = []
+    for n in prog.nodes:
+        if isinstance(n, TI.Elementwise1D):
+            n.inputs = tuple(TI.InputBinding(b.name, remap(b.source)) for b in n.inputs)
+        elif isinstance(n.source, TI.PlainInput):
+            n.source = TI.PlainInput(remap(n.source.input))
+        else:
+            _with_mapped(n, inputs=tuple(TI.InputBinding(b.name, remap(b.source))
+                                         for b in n.source.inputs))
+        key = _node_key(n)
+        if key in seen:
+            redirects[n.id] = TI.NodeRef(seen[key])
+            continue
+        seen[key] = n.id
+        keep.append(n)
+    prog.nodes = keep
+    prog.result = remap(prog.result)
+    return prog
+
+
+TENSOR_BODY_FLAGS = ("tensor-canonicalize", "reduction-input-simplify", "reduction-body-normalize",
+                     "reduction-accumulator-shape", "reduction-reuse-hoist",
+                     "branchy-reduction-rescue", "reduction-body-canonicalize",
+                     "reduction-body-cse", "tensor-cse")
+
+
+def _body_passes(prog: TI.Program, enabled) -> TI.Program:
+    if _on(enabled, "tensor-canonicalize"):
+        prog = canonicalize_program(prog)
+    if _on(enabled, "reduction-input-simplify"):
+        prog = simplify_program(prog)
+    if _on(enabled, "reduction-body-normalize") or _on(enabled, "reduction-accumulator-shape"):
+        prog = reduction_body_normalize(prog)
+    if _on(enabled, "reduction-reuse-hoist"):
+        prog = reduction_reuse_hoist(prog)
+    if _on(enabled, "branchy-reduction-rescue"):
+        prog = branchy_reduction_rescue(prog)
+    if _on(enabled, "reduction-body-canonicalize"):
+        prog = reduction_body_canonicalize(prog)
+    if _on(enabled, "reduction-body-cse"):
+        prog = reduction_body_cse(prog)
+    return prog
+
+
 def apply_tensor_passes(prog: TI.Program, enabled: Sequence[str]) -> TI.Program:
-    """The restated passes in the reference's order (tensor_passes.ml:595-620)."""
+    """The restated passes in the reference's order (tensor_passes.ml:554-666):
+    the body rewrites, fusion, dead-node removal, node CSE, then the body
+    rewrites once more."""
     enabled = tuple(enabled)
+    prog = _body_passes(prog, enabled)
     clone = _on(enabled, "small-producer-clone")
     if any(_on(enabled, f) for f in FUSE_FLAGS):
         prog = fuse_program(prog, enabled, allow_clone=clone)
@@ -275,4 +444,6 @@ def apply_tensor_passes(prog: TI.Program, enabled: Sequence[str]) -> TI.Program:
         prog = reduce_map_fusion_program(prog, enabled, allow_clone=clone)
     if _on(enabled, "shape-use-simplify"):
         prog = shape_use_simplify(prog)
-    return prog
+    if _on(enabled, "tensor-cse"):
+        prog = tensor_cse(prog)
+    return _body_passes(prog, enabled)

@@ -8,9 +8,9 @@ its JSON form follow the reference's ``src/loom_core/tensor_ir.mli:1-114``
 ``tensor_ir.json`` written by ``loomc ... --emit tensor-ir`` loads here
 unchanged, and a program written here reads back in the reference.
 
-Scalar expressions are frozen dataclasses: structural equality (``==``) is
-what the reference's OCaml pattern guards use (``lhs = then_expr`` and the
-like), and the renderer relies on it.
+Scalar expressions are frozen dataclasses whose ``==`` is OCaml's
+structural ``=`` (``expr_eq``), which the reference's pattern guards use
+(``lhs = then_expr`` and the like) and the renderer and passes rely on.
 """
 
 from __future__ import annotations
@@ -29,49 +29,93 @@ BINARY_OPS = ("add", "sub", "mul", "div", "min", "max",
 COMPARE_OPS = ("cmplt", "cmple", "cmpgt", "cmpge", "cmpeq")
 
 
-@dataclass(frozen=True)
-class SVar:
+class _Expr:
+    """Equality of scalar expressions is OCaml's structural ``=``
+    (``expr_eq``); the hash agrees with it."""
+
+    __slots__ = ()
+
+    def __eq__(self, other):
+        return expr_eq(self, other)
+
+    def __ne__(self, other):
+        return not expr_eq(self, other)
+
+    def __hash__(self):
+        return hash(_expr_key(self))
+
+
+@dataclass(frozen=True, eq=False)
+class SVar(_Expr):
     name: str
 
 
-@dataclass(frozen=True)
-class SConstF32:
+@dataclass(frozen=True, eq=False)
+class SConstF32(_Expr):
     # The reference stores the literal as an OCaml float (a double); the
     # CUDA renderer prints it with "%.12g", so keep the double here.
     value: float
 
-    def __eq__(self, other):
-        # OCaml's structural `=` compares floats as IEEE values: -0.0 = 0.0,
-        # and a NaN equals nothing (the reference's pattern guards use it)
-        return isinstance(other, SConstF32) and self.value == other.value
 
-    def __hash__(self):
-        return hash(("f32", self.value))
-
-
-@dataclass(frozen=True)
-class SConstBool:
+@dataclass(frozen=True, eq=False)
+class SConstBool(_Expr):
     value: bool
 
 
-@dataclass(frozen=True)
-class SUnary:
+@dataclass(frozen=True, eq=False)
+class SUnary(_Expr):
     op: str
     expr: "ScalarExpr"
 
 
-@dataclass(frozen=True)
-class SBinary:
+@dataclass(frozen=True, eq=False)
+class SBinary(_Expr):
     op: str
     lhs: "ScalarExpr"
     rhs: "ScalarExpr"
 
 
-@dataclass(frozen=True)
-class SSelect:
+@dataclass(frozen=True, eq=False)
+class SSelect(_Expr):
     cond: "ScalarExpr"
     then: "ScalarExpr"
     els: "ScalarExpr"
+
+
+def expr_eq(a, b) -> bool:
+    """OCaml's structural ``=`` on two scalar expressions: constructors and
+    fields compared recursively, floats as IEEE values (-0.0 = 0.0, a NaN
+    equals nothing, not even itself -- Python's tuple comparison would let
+    one NaN object equal itself, so no tuple comparison is used here)."""
+    if type(a) is not type(b):
+        return False
+    if isinstance(a, SConstF32):
+        return a.value == b.value
+    if isinstance(a, SVar):
+        return a.name == b.name
+    if isinstance(a, SConstBool):
+        return a.value == b.value
+    if isinstance(a, SUnary):
+        return a.op == b.op and expr_eq(a.expr, b.expr)
+    if isinstance(a, SBinary):
+        return a.op == b.op and expr_eq(a.lhs, b.lhs) and expr_eq(a.rhs, b.rhs)
+    if isinstance(a, SSelect):
+        return expr_eq(a.cond, b.cond) and expr_eq(a.then, b.then) and expr_eq(a.els, b.els)
+    return a == b
+
+
+def _expr_key(e):
+    if isinstance(e, SConstF32):
+        return ("f", e.value)          # hash(-0.0) == hash(0.0)
+    if isinstance(e, SVar):
+        return ("v", e.name)
+    if isinstance(e, SConstBool):
+        return ("b", e.value)
+    if isinstance(e, SUnary):
+        return ("u", e.op, _expr_key(e.expr))
+    if isinstance(e, SBinary):
+        return ("b2", e.op, _expr_key(e.lhs), _expr_key(e.rhs))
+    return ("s", _expr_key(e.cond), _expr_key(e.then), _expr_key(e.els))
 
 
 ScalarExpr = Union[SVar, SConstF32, SConstBool, SUnary, SBinary, SSelect]

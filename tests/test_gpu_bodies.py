@@ -4,11 +4,14 @@ thresholds, sqrt, exp/log, division, select, negation, a tail if statement,
 qualified primitives, unary plus and equality, maxes over maps and
 multi-node chains (tests/golden/sources/cases/frontend_cases.py).
 
-The project is packaged twice: with the reference's default flags, and with
-the flags that change how map bodies are rendered (soft-threshold and
+The project is packaged four times: with the reference's default flags;
+with the flags that change how map bodies are rendered (soft-threshold and
 predicated-select rewrites, the `if` clamp form, `__fdividef` for ratio
-bodies; loom_b200.build.RENDER_FLAGS), each checked against the oracle built
-with the same flags.
+bodies; loom_b200.build.RENDER_FLAGS); with the TensorIR fusion passes; and
+with the whole flag set of the reference harness's tuned CUDA profile
+(loom_b200.build.CUDA_FIXED_FLAGS: the scalar and TensorIR rewrites too),
+each checked against the oracle built from the same rewritten programs and
+flags.
 
 Bar: maps and max bit-exact, except `ratio_exp`, whose expf/logf are CUDA's
 (up to 2 ulp / 1 ulp from the correctly rounded value; with the flags also
@@ -25,7 +28,7 @@ import pytest
 import torch
 
 from loom_b200 import tensor_ir as TI
-from loom_b200.build import FUSION_FLAGS, RENDER_FLAGS, build_project
+from loom_b200.build import CUDA_FIXED_FLAGS, FUSION_FLAGS, RENDER_FLAGS, build_project
 from loom_b200.frontend import python_programs
 from loom_b200.loader import Package
 
@@ -39,7 +42,7 @@ SCALARS = {"lo": -0.5, "hi": 0.75, "s": 1.5, "a": 0.3, "t": 0.25, "k": 0.4}
 SCALARS_BY_ENTRY = {"scaled_chain": {"a": 1.25}}
 
 
-@pytest.fixture(scope="module", params=["default", "render_flags", "fusion"])
+@pytest.fixture(scope="module", params=["default", "render_flags", "fusion", "cuda_fixed"])
 def cases(request):
     from oracle.loom_oracle import Oracle
     src = os.path.join(CASES, "frontend_cases.py")
@@ -52,13 +55,19 @@ def cases(request):
         pkg = Package(build_project(CASES, enabled=RENDER_FLAGS, name="frontend_cases_flags"))
         oracle = Oracle([TI.program_to_json(p) for p in progs], name="frontend_cases_flags",
                         enabled=RENDER_FLAGS)
-    else:
+    elif request.param == "fusion":
         # the reference's TensorIR fusion passes ahead of the backend: the
         # oracle evaluates the same fused programs
         progs = python_programs(src, FUSION_FLAGS)
         pkg = Package(build_project(CASES, enabled=FUSION_FLAGS, name="frontend_cases_fused"))
         oracle = Oracle([TI.program_to_json(p) for p in progs], name="frontend_cases_fused",
                         enabled=FUSION_FLAGS)
+    else:
+        progs = python_programs(src, CUDA_FIXED_FLAGS)
+        pkg = Package(build_project(CASES, enabled=CUDA_FIXED_FLAGS,
+                                    name="frontend_cases_cuda_fixed"))
+        oracle = Oracle([TI.program_to_json(p) for p in progs],
+                        name="frontend_cases_cuda_fixed", enabled=CUDA_FIXED_FLAGS)
     return pkg, oracle, {p.entry_name: p for p in progs}
 
 

@@ -10,9 +10,11 @@ is lowered (normalize, tensorize), packaged for sm_100a and run:
 * CPU: every kernel lowers to valid TensorIR, the package finds all 33
   entries, and the oracle compiles them;
 * GPU: every kernel against the oracle on the harness's input distribution
-  (N(0,1) tensors, the harness's scalar arguments), built twice: with the
-  default flags, and with the reference's fusion passes and body-rendering
-  flags (loom_b200.build.FUSION_FLAGS + RENDER_FLAGS).  Maps bit-exact (NaN
+  (N(0,1) tensors, the harness's scalar arguments), built three times: with
+  the default flags, with the reference's fusion passes and body-rendering
+  flags (loom_b200.build.FUSION_FLAGS + RENDER_FLAGS), and with the flag set
+  of the harness's tuned CUDA profile (loom_b200.build.CUDA_FIXED_FLAGS,
+  which adds the scalar and TensorIR rewrites).  Maps bit-exact (NaN
   only has to be NaN), except bodies rendered with __fdividef, which are
   within 2 ulp of the oracle's exact division and are compared at rtol 1e-6;
   sums within 1e-6 * max(1, log2 n) * max(|ref|,
@@ -31,7 +33,7 @@ import pytest
 
 from loom_b200 import tensor_ir as TI
 from loom_b200.artifact import discover_entries, load_front_ir_file
-from loom_b200.build import FUSION_FLAGS, RENDER_FLAGS
+from loom_b200.build import CUDA_FIXED_FLAGS, FUSION_FLAGS, RENDER_FLAGS
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 WL_DIR = os.path.join(HERE, "golden", "sources", "workloads")
@@ -70,7 +72,8 @@ def test_fixtures_cover_the_harness_kernels():
     assert all(w["front_ir_matches_this_front_end"] for w in TABLE)
 
 
-@pytest.mark.parametrize("enabled", [(), FLAGGED], ids=["default", "flags"])
+@pytest.mark.parametrize("enabled", [(), FLAGGED, tuple(CUDA_FIXED_FLAGS)],
+                         ids=["default", "flags", "cuda_fixed"])
 def test_workloads_lower_and_package(enabled):
     progs = _programs(enabled)
     assert len(progs) == 33
@@ -98,8 +101,12 @@ def _inputs(w, n, seed):
     return inp
 
 
+VARIANTS = {"default": ((), "workloads"), "flags": (FLAGGED, "workloads_flags"),
+            "cuda_fixed": (tuple(CUDA_FIXED_FLAGS), "workloads_cuda_fixed")}
+
+
 @pytest.mark.gpu
-@pytest.mark.parametrize("variant", ["default", "flags"])
+@pytest.mark.parametrize("variant", sorted(VARIANTS))
 def test_workloads_match_oracle(variant):
     import torch
 
@@ -108,8 +115,7 @@ def test_workloads_match_oracle(variant):
     from oracle.loom_oracle import Oracle
     from test_gpu_parity import assert_bits, to_device
 
-    enabled = () if variant == "default" else FLAGGED
-    name = "workloads" if variant == "default" else "workloads_flags"
+    enabled, name = VARIANTS[variant]
     progs = _programs(enabled)
     pkg_dir = build_project(WL_DIR, enabled=enabled, name=name)
     pkg = Package(pkg_dir)
