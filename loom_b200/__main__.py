@@ -5,8 +5,8 @@
                                 [--module M ...] [--entry E ...]
                                 [--enable-opt FLAG ...] [--no-multi-gpu]
     python -m loom_b200 compile FILE --entry E --target cuda --out OUT
+                                [--emit KIND] [--enable-opt FLAG ...]
                                 [--input-kind auto|python|front-ir|tensor-ir]
-                                [--enable-opt FLAG ...]
 
 Entries are read from ``*.tensor_ir.json`` files (the TensorIR the reference
 front end dumps with ``--emit tensor-ir``), from ``*.front_ir.json`` files
@@ -75,7 +75,8 @@ def main(argv=None) -> int:
             res = artifact.generate_package(ns.project, ns.out, _options(ns), ns.module, ns.entry)
         else:
             res = artifact.compile_entry(ns.file, ns.entry, ns.out, _options(ns),
-                                         input_kind=ns.input_kind)
+                                         input_kind=ns.input_kind,
+                                         emit=artifact.parse_emit(ns.emit))
     except (TensorIRError, FrontendError, artifact.BuildError) as exc:
         print(f"error: {exc}", file=sys.stderr)
         return 1

@@ -28,7 +28,8 @@ from typing import Iterable, List, Optional, Sequence
 
 from . import codegen
 from .plan import EntryPlan, plan_entry, plan_to_json, sanitize_ident
-from .tensor_ir import Program, TensorIRError, program_from_json, program_to_string
+from .tensor_ir import (Program, TensorIRError, program_from_json, program_to_json,
+                        program_to_string)
 
 CSRC = Path(__file__).resolve().parent / "csrc"
 CUDA_ARCH = "sm_100a"
@@ -93,6 +94,10 @@ class EntryBundle:
     source_file: str
     program: Program
     plan: EntryPlan
+    # the FrontIR and LoomLambda entries it was lowered from (None for a
+    # TensorIR source)
+    front_ir: Optional[dict] = None
+    loom_lambda: Optional[dict] = None
 
 
 def module_name_of_file(path: str) -> str:
@@ -123,10 +128,14 @@ def load_front_ir_file(path: str, enabled: Sequence[str] = ()) -> List[Program]:
     frontend writes it (``loomc compile --input-kind front-ir``,
     ``src/loom_cli/main.ml:219-226``), lowered through normalize and
     tensorize here."""
-    from .frontend import program_from_front_ir
+    return [prog for _, _, prog in _front_ir_file_stages(path, enabled)]
+
+
+def _front_ir_file_stages(path: str, enabled: Sequence[str]):
+    from .frontend import front_ir_stages
     with open(path, "r", encoding="utf-8") as fh:
         obj = json.load(fh)
-    return [program_from_front_ir(e, enabled) for e in (obj if isinstance(obj, list) else [obj])]
+    return [front_ir_stages(e, enabled) for e in (obj if isinstance(obj, list) else [obj])]
 
 
 def load_source_file(path: str, enabled: Sequence[str] = (), kind: str = "auto") -> List[Program]:
@@ -135,16 +144,23 @@ def load_source_file(path: str, enabled: Sequence[str] = (), kind: str = "auto")
     module of ``@loom.entry`` functions (through the front end); the last two
     with the TensorIR passes `enabled` switches on.  `kind` ("python",
     "front-ir", "tensor-ir") overrides the choice by file name."""
+    return [prog for _, _, prog in load_source_stages(path, enabled, kind)]
+
+
+def load_source_stages(path: str, enabled: Sequence[str] = (), kind: str = "auto"):
+    """As ``load_source_file``, with each program's FrontIR and LoomLambda
+    entries: ``(front_ir, loom_lambda, program)``, the first two None for a
+    TensorIR source."""
     if kind == "auto":
         kind = ("python" if path.endswith(".py") else
                 "front-ir" if path.endswith(".front_ir.json") else "tensor-ir")
     if kind == "python":
-        from .frontend import python_programs
-        return python_programs(path, enabled)
+        from .frontend import python_stages
+        return python_stages(path, enabled)
     if kind == "front-ir":
-        return load_front_ir_file(path, enabled)
+        return _front_ir_file_stages(path, enabled)
     if kind == "tensor-ir":
-        return load_entries_file(path)
+        return [(None, None, prog) for prog in load_entries_file(path)]
     raise TensorIRError(f"unknown input kind {kind!r} (expected python, front-ir or tensor-ir)")
 
 
@@ -171,10 +187,11 @@ def discover_entries(project_root: str, module_filters: Sequence[str] = (),
         module = module_name_of_file(path)
         if mfilt and module.lower() not in mfilt:
             continue
-        for prog in load_source_file(path, enabled):
+        for front, lam, prog in load_source_stages(path, enabled):
             if efilt and prog.entry_name.lower() not in efilt:
                 continue
-            bundles.append(EntryBundle(module, path, prog, plan_entry(prog, module, enabled)))
+            bundles.append(EntryBundle(module, path, prog, plan_entry(prog, module, enabled),
+                                       front, lam))
     return bundles
 
 
@@ -322,19 +339,29 @@ def _write(path: str, text: str) -> None:
         fh.write(text)
 
 
+def _backend_analysis(b: EntryBundle) -> str:
+    return json.dumps({
+        "entry_name": b.program.entry_name,
+        "hbm_bytes_per_element": b.plan.bytes_per_element,
+        "roofline": "hbm",
+        "tensor_slots": b.plan.slots,
+    }, indent=2)
+
+
 def _write_entry_dir(out_dir: str, b: EntryBundle) -> List[str]:
+    """``entries/<symbol>/`` (cuda_backend.ml:2272-2313): the OCaml raw
+    lambda is unavailable (no OCaml frontend here); the LoomLambda is
+    written when the entry came from a Python or FrontIR source."""
     sym = b.plan.symbol
     rel = os.path.join("entries", sym)
-    files = {
+    files = {"lambda.sexp": "; unavailable\n"}
+    if b.loom_lambda is not None:
+        files["loom_lambda.json"] = json.dumps(b.loom_lambda, indent=2)
+    files.update({
         "tensor_ir.json": program_to_string(b.program),
-        "cuda_plan.json": json.dumps(plan_to_json(b.plan), indent=2),
         "kernel_plan.json": json.dumps(plan_to_json(b.plan), indent=2),
-        "backend_analysis.json": json.dumps({
-            "entry_name": b.program.entry_name,
-            "hbm_bytes_per_element": b.plan.bytes_per_element,
-            "roofline": "hbm",
-            "tensor_slots": b.plan.slots,
-        }, indent=2),
+        "cuda_plan.json": json.dumps(plan_to_json(b.plan), indent=2),
+        "backend_analysis.json": _backend_analysis(b),
         "report.md": "\n".join([
             "# Loom Entry Report", "",
             f"- entrypoint: `{b.program.entry_name}`",
@@ -346,7 +373,7 @@ def _write_entry_dir(out_dir: str, b: EntryBundle) -> List[str]:
             f"- result kind: `{b.program.result_kind}`",
             "- generated kernels: `1`",
             "- temporary allocations: `0`", ""]),
-    }
+    })
     out = []
     for name, text in files.items():
         _write(os.path.join(out_dir, rel, name), text)
@@ -403,20 +430,61 @@ def generate_package(project_root: str, out_dir: str, opts: Optional[Options] = 
                          commands)
 
 
+# `loomc compile --emit <kind>` (src/loom_cli/main.ml:53-67); "all" is every
+# kind the CUDA target writes (:241-268)
+EMIT_KINDS = ("front-ir", "lambda", "loom-lambda", "tensor-ir", "kernel-plan", "cuda-plan",
+              "backend-analysis", "cuda", "report")
+
+
+def parse_emit(value: str) -> List[str]:
+    """The kinds one ``--emit`` value selects, with the reference's errors
+    (main.ml:53-67, 78-112)."""
+    if value in ("triton-plan", "triton"):
+        raise BuildError(f"--emit {value} cannot be used with --target cuda")
+    if value == "all":
+        return list(EMIT_KINDS)
+    if value not in EMIT_KINDS:
+        raise BuildError(f"unknown emit target {value}")
+    return [value]
+
+
 def compile_entry(source_file: str, entry_name: str, out_dir: str,
                   opts: Optional[Options] = None, build: bool = True,
-                  input_kind: str = "auto") -> PackageResult:
-    """``loomc compile <file> --entry e --target cuda`` (cuda_backend.ml:2675-2731)."""
+                  input_kind: str = "auto", emit: Sequence[str] = EMIT_KINDS) -> PackageResult:
+    """``loomc compile <file> --entry e --target cuda`` (src/loom_cli/main.ml:228-330,
+    cuda_backend.ml:2675-2731): the IR dumps that `emit` selects, then
+    ``pipeline.json`` and the header, source, library, manifest and report
+    that the CUDA target always writes.  ``lambda.sexp`` says the OCaml raw
+    lambda is unavailable, as the reference says for its non-OCaml
+    frontends; ``front_ir.json`` and ``loom_lambda.json`` need a Python or
+    FrontIR source."""
     opts = opts or Options()
     module = module_name_of_file(source_file)
-    progs = [p for p in load_source_file(source_file, opts.enabled, input_kind)
-             if p.entry_name == entry_name]
-    if not progs:
+    stages = [st for st in load_source_stages(source_file, opts.enabled, input_kind)
+              if st[2].entry_name == entry_name]
+    if not stages:
         raise TensorIRError(f"entry {entry_name!r} not found in {source_file}")
-    prog = progs[0]
+    front, lam, prog = stages[0]
     b = EntryBundle(module, os.path.abspath(source_file), prog,
-                    plan_entry(prog, module, opts.enabled))
+                    plan_entry(prog, module, opts.enabled), front, lam)
     out_dir = os.path.abspath(out_dir)
+    plan_text = json.dumps(plan_to_json(b.plan), indent=2)
+    dumps = {"front-ir": ("front_ir.json", None if front is None else json.dumps(front, indent=2)),
+             "lambda": ("lambda.sexp", "; unavailable for this frontend\n"),
+             "loom-lambda": ("loom_lambda.json",
+                             None if lam is None else json.dumps(lam, indent=2)),
+             "tensor-ir": ("tensor_ir.json", program_to_string(prog)),
+             "kernel-plan": ("kernel_plan.json", plan_text),
+             "cuda-plan": ("cuda_plan.json", plan_text),
+             "backend-analysis": ("backend_analysis.json", _backend_analysis(b))}
+    for kind in emit:
+        name, text = dumps.get(kind, (None, None))
+        if text is not None:
+            _write(os.path.join(out_dir, name), text)
+    _write(os.path.join(out_dir, "pipeline.json"), json.dumps({
+        "front_ir": front, "loom_lambda": lam, "tensor_ir": program_to_json(prog),
+        "kernel_plan": plan_to_json(b.plan), "cuda_plan": plan_to_json(b.plan),
+        "optimizations": opts.to_json()}, indent=2))
     header = os.path.join(out_dir, f"{entry_name}_cuda.h")
     source = os.path.join(out_dir, f"{entry_name}_cuda.cu")
     artifact = os.path.join(out_dir, f"lib{entry_name}.so")
@@ -424,8 +492,6 @@ def compile_entry(source_file: str, entry_name: str, out_dir: str,
     _write(header, codegen.render_header(package, [b.plan], opts.multi_gpu))
     _write(source, codegen.render_source(package, os.path.basename(header), [b.plan],
                                          opts.async_return, opts.multi_gpu))
-    _write(os.path.join(out_dir, "tensor_ir.json"), program_to_string(prog))
-    _write(os.path.join(out_dir, "cuda_plan.json"), json.dumps(plan_to_json(b.plan), indent=2))
     commands = build_artifact(opts, out_dir, source, artifact) if build else \
         [shlex.join(nvcc_command(opts, out_dir, source, artifact))]
     files = [os.path.basename(p) for p in (header, source, artifact)]

@@ -11,14 +11,27 @@ from .lower import loom_lambda, program_from_front_ir, tensor_ir
 from .python_front import FrontendError, front_ir, list_entries
 
 
-def python_programs(path: str, enabled=()) -> List[TI.Program]:
-    """Every ``@loom.entry`` of a Python source file, lowered to TensorIR
-    (with the TensorIR passes that the flags in `enabled` switch on)."""
+def front_ir_stages(front: dict, enabled=()) -> Tuple[dict, dict, TI.Program]:
+    """One FrontIR entry through normalize and tensorize: (FrontIR,
+    LoomLambda, TensorIR), with the passes that `enabled` switches on."""
+    lam = loom_lambda(front, enabled)
+    return front, lam, tensor_ir(lam, enabled)
+
+
+def python_stages(path: str, enabled=()) -> List[Tuple[dict, dict, TI.Program]]:
+    """Every ``@loom.entry`` of a Python source file: its FrontIR, LoomLambda
+    and TensorIR."""
     with open(path, "r", encoding="utf-8") as fh:
         src = fh.read()
-    return [program_from_front_ir(front_ir(src, e["name"], path), enabled)
+    return [front_ir_stages(front_ir(src, e["name"], path), enabled)
             for e in list_entries(src, path)]
 
 
+def python_programs(path: str, enabled=()) -> List[TI.Program]:
+    """Every ``@loom.entry`` of a Python source file, lowered to TensorIR
+    (with the TensorIR passes that the flags in `enabled` switch on)."""
+    return [prog for _, _, prog in python_stages(path, enabled)]
+
+
 __all__ = ["FrontendError", "front_ir", "list_entries", "loom_lambda", "tensor_ir",
-           "program_from_front_ir", "python_programs"]
+           "program_from_front_ir", "front_ir_stages", "python_stages", "python_programs"]

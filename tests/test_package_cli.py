@@ -180,3 +180,56 @@ def test_async_wrapper_return_results_after_synchronise(async_package):
     torch.cuda.synchronize()
     torch.testing.assert_close(s[0], torch.sum(x.double() * y.double()).float(),
                                rtol=1e-5, atol=1e-4)
+
+
+def _compile(*args):
+    return subprocess.run([sys.executable, "-m", "loom_b200", "compile", *args], cwd=ROOT,
+                          capture_output=True, text=True)
+
+
+def test_compile_emits_the_reference_artifact_set(tmp_path):
+    # test/python/test_cli.py:328-368 (the CUDA target with --emit all)
+    (tmp_path / "kernels.py").write_text(KERNELS)
+    out = tmp_path / "out"
+    result = _compile(str(tmp_path / "kernels.py"), "--entry", "saxpy", "--target", "cuda",
+                      "--out", str(out), "--emit", "all")
+    assert result.returncode == 0, result.stderr
+    expected = {"front_ir.json", "lambda.sexp", "loom_lambda.json", "tensor_ir.json",
+                "kernel_plan.json", "cuda_plan.json", "backend_analysis.json", "pipeline.json",
+                "manifest.json", "report.md", "saxpy_cuda.cu", "saxpy_cuda.h", "libsaxpy.so"}
+    assert expected <= {p.name for p in out.iterdir()}
+    manifest = json.loads((out / "manifest.json").read_text())
+    assert manifest["target_backend"] == "cuda" and manifest["mode"] == "compile"
+    assert [e["entry_name"] for e in manifest["entries"]] == ["saxpy"]
+    assert manifest["entries"][0]["result_kind"] == "tensor"
+    pipeline = json.loads((out / "pipeline.json").read_text())
+    assert {"front_ir", "loom_lambda", "tensor_ir", "kernel_plan", "cuda_plan"} <= set(pipeline)
+    assert pipeline["loom_lambda"] == json.loads((out / "loom_lambda.json").read_text())
+    assert pipeline["loom_lambda"]["entry"] == "saxpy"
+    # test/python/test_cli.py:198: non-OCaml frontends have no raw lambda
+    assert "unavailable for this frontend" in (out / "lambda.sexp").read_text()
+
+
+def test_compile_emit_selects_dumps_and_rejects_triton_kinds(tmp_path):
+    (tmp_path / "kernels.py").write_text(KERNELS)
+    out = tmp_path / "only_tir"
+    result = _compile(str(tmp_path / "kernels.py"), "--entry", "dot", "--target", "cuda",
+                      "--out", str(out), "--emit", "tensor-ir")
+    assert result.returncode == 0, result.stderr
+    names = {p.name for p in out.iterdir()}
+    assert "tensor_ir.json" in names and "pipeline.json" in names and "libdot.so" in names
+    assert not names & {"front_ir.json", "loom_lambda.json", "kernel_plan.json", "cuda_plan.json"}
+    # test/python/test_cli.py:284-301
+    result = _compile(str(tmp_path / "kernels.py"), "--entry", "dot", "--target", "cuda",
+                      "--out", str(tmp_path / "bad"), "--emit", "triton-plan")
+    assert result.returncode != 0
+    assert "--emit triton-plan cannot be used with --target cuda" in result.stderr
+
+
+def test_package_entry_dirs_hold_the_loom_lambda(shared_package):
+    # cuda_backend.ml:2272-2313: lambda.sexp and loom_lambda.json beside the
+    # TensorIR of every entry
+    d = shared_package / "entries" / "loom_kernels_saxpy"
+    assert (d / "lambda.sexp").read_text() == "; unavailable\n"
+    lam = json.loads((d / "loom_lambda.json").read_text())
+    assert lam["entry"] == "saxpy" and lam["body"]["kind"] == "tensor-prim"
