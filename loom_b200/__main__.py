@@ -7,6 +7,8 @@
     python -m loom_b200 compile FILE --entry E --target cuda --out OUT
                                 [--emit KIND] [--enable-opt FLAG ...]
                                 [--input-kind auto|python|front-ir|tensor-ir]
+    python -m loom_b200 list-entries FILE [--input-kind python]
+    python -m loom_b200 front-ir FILE --entry E [--input-kind python]
 
 Entries are read from ``*.tensor_ir.json`` files (the TensorIR the reference
 front end dumps with ``--emit tensor-ir``), from ``*.front_ir.json`` files
@@ -38,6 +40,52 @@ def _options(ns) -> artifact.Options:
                             kind=getattr(ns, "kind", "shared"))
 
 
+def _input_kind(value: str) -> str:
+    """``--input-kind`` with the reference's spellings (main.ml:143-151)."""
+    v = value.lower()
+    kind = {"py": "python", "front_ir": "front-ir", "c++": "cpp"}.get(v, v)
+    if kind not in ("auto", "python", "front-ir", "tensor-ir", "ocaml", "cpp"):
+        raise artifact.BuildError(f"unknown input kind {value} (expected ocaml, python, cpp, "
+                                  "or front-ir)")
+    if kind in ("ocaml", "cpp"):
+        raise artifact.BuildError(f"--input-kind {kind}: this backend reads Python, FrontIR "
+                                  "and TensorIR sources (the OCaml and C++ frontends write "
+                                  "FrontIR, which --input-kind front-ir takes)")
+    return kind
+
+
+def _read_python(path: str, kind: str, command: str) -> str:
+    """The Python source that ``list-entries`` and ``front-ir`` read; a
+    FrontIR input is refused with the reference's message (main.ml:191,
+    :335)."""
+    if kind == "front-ir":
+        raise artifact.BuildError(f"{command} does not support --input-kind front-ir")
+    if kind == "tensor-ir" or (kind == "auto" and not path.endswith(".py")):
+        raise artifact.BuildError(f"{command} reads Python sources")
+    with open(path, "r", encoding="utf-8") as fh:
+        return fh.read()
+
+
+def list_entries(path: str, kind: str) -> int:
+    """``loomc list-entries`` (main.ml:166-201): one line per entry,
+    ``name (param:kind, ...)``."""
+    from .frontend import list_entries as entries
+    src = _read_python(path, kind, "list-entries")
+    for e in entries(src, path):
+        params = ", ".join(f"{p['name']}:{p['kind']}" for p in e["params"])
+        print(f"{e['name']} ({params})")
+    return 0
+
+
+def emit_front_ir(path: str, entry: str, kind: str) -> int:
+    """``loomc front-ir`` (main.ml:332-338): the entry's FrontIR as JSON."""
+    import json
+    from .frontend import front_ir
+    src = _read_python(path, kind, "front-ir command")
+    print(json.dumps(front_ir(src, entry, path), indent=2))
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="python -m loom_b200")
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -62,11 +110,27 @@ def main(argv=None) -> int:
     cp.add_argument("file")
     cp.add_argument("--entry", required=True)
     cp.add_argument("--emit", default="all")
-    cp.add_argument("--input-kind", default="auto",
-                    choices=["auto", "python", "front-ir", "tensor-ir"])
+    cp.add_argument("--input-kind", default="auto")
     common(cp)
 
+    le = sub.add_parser("list-entries", help="list the entries of a Python source")
+    le.add_argument("file")
+    le.add_argument("--input-kind", default="auto")
+
+    fi = sub.add_parser("front-ir", help="print an entry's FrontIR")
+    fi.add_argument("file")
+    fi.add_argument("--entry", required=True)
+    fi.add_argument("--input-kind", default="auto")
+
     ns = ap.parse_args(argv)
+    try:
+        if ns.cmd == "list-entries":
+            return list_entries(ns.file, _input_kind(ns.input_kind))
+        if ns.cmd == "front-ir":
+            return emit_front_ir(ns.file, ns.entry, _input_kind(ns.input_kind))
+    except (FrontendError, artifact.BuildError, OSError) as exc:
+        print(f"error: {exc}", file=sys.stderr)
+        return 1
     if ns.cuda_arch not in ("sm_100a", "sm_100"):
         print(f"error: this backend targets sm_100a only (got {ns.cuda_arch})", file=sys.stderr)
         return 2
@@ -75,7 +139,7 @@ def main(argv=None) -> int:
             res = artifact.generate_package(ns.project, ns.out, _options(ns), ns.module, ns.entry)
         else:
             res = artifact.compile_entry(ns.file, ns.entry, ns.out, _options(ns),
-                                         input_kind=ns.input_kind,
+                                         input_kind=_input_kind(ns.input_kind),
                                          emit=artifact.parse_emit(ns.emit))
     except (TensorIRError, FrontendError, artifact.BuildError) as exc:
         print(f"error: {exc}", file=sys.stderr)

@@ -460,8 +460,14 @@ def compile_entry(source_file: str, entry_name: str, out_dir: str,
     FrontIR source."""
     opts = opts or Options()
     module = module_name_of_file(source_file)
-    stages = [st for st in load_source_stages(source_file, opts.enabled, input_kind)
-              if st[2].entry_name == entry_name]
+    loaded = load_source_stages(source_file, opts.enabled, input_kind)
+    stages = [st for st in loaded if st[2].entry_name == entry_name]
+    front_ir_file = input_kind == "front-ir" or (
+        input_kind == "auto" and source_file.endswith(".front_ir.json"))
+    if not stages and front_ir_file and len(loaded) == 1:
+        # main.ml:219-226: a FrontIR file holds one entry, which must be the one asked for
+        raise TensorIRError(f"FrontIR entry {loaded[0][0]['entry']} does not match requested "
+                            f"--entry {entry_name}")
     if not stages:
         raise TensorIRError(f"entry {entry_name!r} not found in {source_file}")
     front, lam, prog = stages[0]

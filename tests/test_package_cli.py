@@ -233,3 +233,31 @@ def test_package_entry_dirs_hold_the_loom_lambda(shared_package):
     assert (d / "lambda.sexp").read_text() == "; unavailable\n"
     lam = json.loads((d / "loom_lambda.json").read_text())
     assert lam["entry"] == "saxpy" and lam["body"]["kind"] == "tensor-prim"
+
+
+def _cli(*args):
+    return subprocess.run([sys.executable, "-m", "loom_b200", *args], cwd=ROOT,
+                          capture_output=True, text=True)
+
+
+def test_list_entries_and_front_ir_commands(tmp_path):
+    # test/python/test_cli.py:75-96
+    src = tmp_path / "kernels.py"
+    src.write_text(KERNELS)
+    result = _cli("list-entries", str(src), "--input-kind", "python")
+    assert result.returncode == 0, result.stderr
+    assert "saxpy (a:scalar-f32, x:tensor1-f32, y:tensor1-f32)" in result.stdout
+    result = _cli("front-ir", str(src), "--input-kind", "py", "--entry", "saxpy")
+    assert result.returncode == 0, result.stderr
+    payload = json.loads(result.stdout)
+    assert payload["entry"] == "saxpy"
+    assert [p["type"] for p in payload["params"]] == ["float", "tensor1<f32>", "tensor1<f32>"]
+    # main.ml:191, :335 and :219-226
+    fir = tmp_path / "saxpy.front_ir.json"
+    fir.write_text(result.stdout)
+    bad = _cli("list-entries", str(fir), "--input-kind", "front-ir")
+    assert bad.returncode != 0
+    assert "list-entries does not support --input-kind front-ir" in bad.stderr
+    bad = _cli("compile", str(fir), "--entry", "relu", "--out", str(tmp_path / "o"))
+    assert bad.returncode != 0
+    assert "FrontIR entry saxpy does not match requested --entry relu" in bad.stderr
