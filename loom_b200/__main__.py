@@ -2,7 +2,7 @@
 (``src/loom_cli/main.ml:305-346``, flags at ``:443-458``):
 
     python -m loom_b200 package --project DIR --out OUT [--kind shared|static]
-                                [--module M ...] [--entry E ...]
+                                [--input-kind auto|python] [--module M ...] [--entry E ...]
                                 [--enable-opt FLAG ...] [--no-multi-gpu]
     python -m loom_b200 compile FILE --entry E --target cuda --out OUT
                                 [--emit KIND] [--enable-opt FLAG ...]
@@ -104,6 +104,7 @@ def main(argv=None) -> int:
     pk.add_argument("--kind", default="shared", choices=["shared", "static"])
     pk.add_argument("--module", action="append", default=[])
     pk.add_argument("--entry", action="append", default=[])
+    pk.add_argument("--input-kind", default="auto")
     common(pk)
 
     cp = sub.add_parser("compile", help="compile one entry")
@@ -136,7 +137,12 @@ def main(argv=None) -> int:
         return 2
     try:
         if ns.cmd == "package":
-            res = artifact.generate_package(ns.project, ns.out, _options(ns), ns.module, ns.entry)
+            kind = _input_kind(ns.input_kind)
+            if kind not in ("auto", "python"):
+                raise artifact.BuildError(f"unknown package input kind {ns.input_kind} "
+                                          "(expected ocaml, python, cpp, or auto)")
+            res = artifact.generate_package(ns.project, ns.out, _options(ns), ns.module,
+                                            ns.entry, input_kind=kind)
         else:
             res = artifact.compile_entry(ns.file, ns.entry, ns.out, _options(ns),
                                          input_kind=_input_kind(ns.input_kind),

@@ -165,19 +165,21 @@ def load_source_stages(path: str, enabled: Sequence[str] = (), kind: str = "auto
 
 
 def discover_entries(project_root: str, module_filters: Sequence[str] = (),
-                     entry_filters: Sequence[str] = (), enabled: Sequence[str] = ()
-                     ) -> List[EntryBundle]:
+                     entry_filters: Sequence[str] = (), enabled: Sequence[str] = (),
+                     input_kind: str = "auto") -> List[EntryBundle]:
     """Collect entries of a project (cuda_backend.ml:158-178, 307-326): every
     ``*.tensor_ir.json``, every ``*.front_ir.json`` and every Python module
-    with ``@loom.entry`` functions below the root, skipping build and hidden
-    dirs, in path order."""
+    with ``@loom.entry`` functions below the root (only the Python modules
+    when `input_kind` is "python"), skipping build and hidden dirs, in path
+    order."""
     skip = {"_build", "build", ".venv", ".git", ".hg", ".svn", "node_modules", "__pycache__"}
     found: List[str] = []
     for dirpath, dirnames, filenames in os.walk(project_root):
         dirnames[:] = sorted(d for d in dirnames if d not in skip and not d.startswith("."))
         for name in sorted(filenames):
             path = os.path.join(dirpath, name)
-            if (name.endswith(".tensor_ir.json") or name.endswith(".front_ir.json")
+            ir_file = name.endswith(".tensor_ir.json") or name.endswith(".front_ir.json")
+            if ((ir_file and input_kind == "auto")
                     or (name.endswith(".py") and _defines_entries(path))):
                 found.append(path)
     mfilt = [m.lower() for m in module_filters]
@@ -395,12 +397,14 @@ class PackageResult:
 
 def generate_package(project_root: str, out_dir: str, opts: Optional[Options] = None,
                      module_filters: Sequence[str] = (), entry_filters: Sequence[str] = (),
-                     build: bool = True, package_name: Optional[str] = None) -> PackageResult:
+                     build: bool = True, package_name: Optional[str] = None,
+                     input_kind: str = "auto") -> PackageResult:
     """``loomc package --target cuda`` (cuda_backend.ml:2733-2816) for B200."""
     opts = opts or Options()
     project_root = os.path.abspath(project_root)
     package = package_name or package_name_of_root(project_root)
-    bundles = discover_entries(project_root, module_filters, entry_filters, opts.enabled)
+    bundles = discover_entries(project_root, module_filters, entry_filters, opts.enabled,
+                               input_kind)
     if not bundles:
         raise TensorIRError("no Loom entries matched the requested project selection")
     symbols = [b.plan.symbol for b in bundles]

@@ -83,7 +83,7 @@ def test_package_static_with_filters(tmp_path):
     proj = _project(tmp_path)
     out = tmp_path / "out"
     result = _package("--project", str(proj), "--out", str(out), "--kind", "static",
-                      "--module", "kernels", "--entry", "relu",
+                      "--input-kind", "python", "--module", "kernels", "--entry", "relu",
                       "--enable-opt", "elementwise-plan-specialize")
     assert result.returncode == 0, result.stderr
     manifest = json.loads((out / "manifest.json").read_text())
