@@ -16,8 +16,7 @@ import math
 from typing import List, Sequence
 
 from .. import tensor_ir as TI
-from .lower import _rank as scalar_rank
-from .lower import body_metrics
+from .lower import body_metrics, scalar_rank
 
 _INF = float("inf")
 _NAN = float("nan")

@@ -321,7 +321,7 @@ class _Tensorizer:
 
 # --- annotation (metrics) ------------------------------------------------------
 
-def _rank(e) -> str:
+def scalar_rank(e) -> str:
     """Structural key of an expression; a unary's operator is not part of it
     (reduction_analysis.ml:3-28)."""
     if isinstance(e, TI.SVar):
@@ -331,10 +331,10 @@ def _rank(e) -> str:
     if isinstance(e, TI.SConstBool):
         return "b:" + ("true" if e.value else "false")
     if isinstance(e, TI.SUnary):
-        return "u:" + _rank(e.expr)
+        return "u:" + scalar_rank(e.expr)
     if isinstance(e, TI.SBinary):
-        return f"b:{e.op}:{_rank(e.lhs)}:{_rank(e.rhs)}"
-    return f"s:{_rank(e.cond)}:{_rank(e.then)}:{_rank(e.els)}"
+        return f"b:{e.op}:{scalar_rank(e.lhs)}:{scalar_rank(e.rhs)}"
+    return f"s:{scalar_rank(e.cond)}:{scalar_rank(e.then)}:{scalar_rank(e.els)}"
 
 
 def _children(e):
@@ -357,7 +357,7 @@ def body_metrics(uses: int, body) -> TI.BodyMetrics:
     def walk(e):
         if isinstance(e, (TI.SVar, TI.SConstF32, TI.SConstBool)):
             return
-        key = _rank(e)
+        key = scalar_rank(e)
         counts[key] = counts.get(key, 0) + 1
         for c in _children(e):
             walk(c)
