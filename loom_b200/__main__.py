@@ -3,10 +3,12 @@
 
     python -m loom_b200 package --project DIR --out OUT [--kind shared|static]
                                 [--input-kind auto|python] [--module M ...] [--entry E ...]
-                                [--enable-opt FLAG ...] [--no-multi-gpu]
+                                [--opt-config PATH] [--enable-opt FLAG ...]
+                                [--disable-opt FLAG ...] [--no-multi-gpu]
     python -m loom_b200 compile FILE --entry E --target cuda --out OUT
-                                [--emit KIND] [--enable-opt FLAG ...]
-                                [--input-kind auto|python|front-ir|tensor-ir]
+                                [--emit KIND] [--input-kind auto|python|front-ir|tensor-ir]
+                                [--opt-config PATH] [--enable-opt FLAG ...]
+                                [--disable-opt FLAG ...]
     python -m loom_b200 list-entries FILE [--input-kind python]
     python -m loom_b200 front-ir FILE --entry E [--input-kind python]
 
@@ -25,19 +27,23 @@ import sys
 
 from . import artifact
 from .frontend import FrontendError
+from .optconfig import DEFAULT_CONFIG, OptionsError, load_config, parse_cli_flags
 from .tensor_ir import TensorIRError
 
 
 def _options(ns) -> artifact.Options:
-    enabled = []
+    """Flags and configuration as loomc reads them (optimization_config.ml:182-206):
+    unknown flag names are errors; --opt-config replaces the default
+    configuration."""
+    enabled, disabled = [], []
     for item in ns.enable_opt or []:
         enabled += [f for f in item.split(",") if f]
-    disabled = set()
     for item in ns.disable_opt or []:
-        disabled |= {f for f in item.split(",") if f}
-    return artifact.Options(enabled=[f for f in enabled if f not in disabled],
+        disabled += [f for f in item.split(",") if f]
+    config = load_config(ns.opt_config) if ns.opt_config else DEFAULT_CONFIG
+    return artifact.Options(enabled=parse_cli_flags(enabled, disabled),
                             multi_gpu=not ns.no_multi_gpu,
-                            kind=getattr(ns, "kind", "shared"))
+                            kind=getattr(ns, "kind", "shared"), config=config)
 
 
 def _input_kind(value: str) -> str:
@@ -95,6 +101,7 @@ def main(argv=None) -> int:
         p.add_argument("--target", default="cuda", choices=["cuda"])
         p.add_argument("--cuda-arch", default="sm_100a")
         p.add_argument("--cuda-platform", default="current")
+        p.add_argument("--opt-config")
         p.add_argument("--enable-opt", action="append")
         p.add_argument("--disable-opt", action="append")
         p.add_argument("--no-multi-gpu", action="store_true")
@@ -147,7 +154,7 @@ def main(argv=None) -> int:
             res = artifact.compile_entry(ns.file, ns.entry, ns.out, _options(ns),
                                          input_kind=_input_kind(ns.input_kind),
                                          emit=artifact.parse_emit(ns.emit))
-    except (TensorIRError, FrontendError, artifact.BuildError) as exc:
+    except (TensorIRError, FrontendError, artifact.BuildError, OptionsError, OSError) as exc:
         print(f"error: {exc}", file=sys.stderr)
         return 1
     print(res.artifact_path)

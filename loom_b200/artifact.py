@@ -27,6 +27,7 @@ from pathlib import Path
 from typing import Iterable, List, Optional, Sequence
 
 from . import codegen
+from .optconfig import DEFAULT_CONFIG, OptConfig, in_catalogue_order
 from .plan import EntryPlan, plan_entry, plan_to_json, sanitize_ident
 from .tensor_ir import (Program, TensorIRError, program_from_json, program_to_json,
                         program_to_string)
@@ -75,17 +76,24 @@ class Options:
     extra_nvcc_flags: List[str] = field(default_factory=list)
     # reduction entries that also get a <sym>_noalloc variant (static scratch)
     noalloc_entries: List[str] = field(default_factory=list)
+    # the tuning configuration (``--opt-config``); its pass thresholds steer
+    # the front end
+    config: OptConfig = DEFAULT_CONFIG
 
     @property
     def async_return(self) -> bool:
         return "cuda-async-wrapper-return" in self.enabled
 
     def to_json(self) -> dict:
-        on = set(self.enabled)
-        return {"enabled": sorted(on),
-                "honoured": sorted(on & HONOURED_FLAGS),
-                "tensor_ir_passes_for_python_sources": sorted(on & FRONTEND_PASS_FLAGS),
-                "no_effect_on_b200_plan": sorted(on - HONOURED_FLAGS - FRONTEND_PASS_FLAGS)}
+        """The reference's ``optimizations`` object (enabled flags in
+        catalogue order, and the configuration; optimization_config.ml:269-274),
+        with what each flag does here."""
+        on = in_catalogue_order(self.enabled)
+        return {"enabled": on, "config": self.config.to_json(),
+                "honoured": [f for f in on if f in HONOURED_FLAGS],
+                "tensor_ir_passes_for_python_sources": [f for f in on if f in FRONTEND_PASS_FLAGS],
+                "no_effect_on_b200_plan": [f for f in on if f not in HONOURED_FLAGS
+                                           and f not in FRONTEND_PASS_FLAGS]}
 
 
 @dataclass
@@ -123,31 +131,34 @@ def _defines_entries(path: str) -> bool:
     return "loom.entry" in text or "@entry" in text
 
 
-def load_front_ir_file(path: str, enabled: Sequence[str] = ()) -> List[Program]:
+def load_front_ir_file(path: str, enabled: Sequence[str] = (),
+                       cfg: OptConfig = DEFAULT_CONFIG) -> List[Program]:
     """A ``*.front_ir.json`` file: one FrontIR entry or a list, as any Loom
     frontend writes it (``loomc compile --input-kind front-ir``,
     ``src/loom_cli/main.ml:219-226``), lowered through normalize and
     tensorize here."""
-    return [prog for _, _, prog in _front_ir_file_stages(path, enabled)]
+    return [prog for _, _, prog in _front_ir_file_stages(path, enabled, cfg)]
 
 
-def _front_ir_file_stages(path: str, enabled: Sequence[str]):
+def _front_ir_file_stages(path: str, enabled: Sequence[str], cfg: OptConfig = DEFAULT_CONFIG):
     from .frontend import front_ir_stages
     with open(path, "r", encoding="utf-8") as fh:
         obj = json.load(fh)
-    return [front_ir_stages(e, enabled) for e in (obj if isinstance(obj, list) else [obj])]
+    return [front_ir_stages(e, enabled, cfg) for e in (obj if isinstance(obj, list) else [obj])]
 
 
-def load_source_file(path: str, enabled: Sequence[str] = (), kind: str = "auto") -> List[Program]:
+def load_source_file(path: str, enabled: Sequence[str] = (), kind: str = "auto",
+                     cfg: OptConfig = DEFAULT_CONFIG) -> List[Program]:
     """Programs of one source: a ``*.tensor_ir.json`` (one program or a list,
     taken as given), a ``*.front_ir.json`` (FrontIR entries), or a Python
     module of ``@loom.entry`` functions (through the front end); the last two
     with the TensorIR passes `enabled` switches on.  `kind` ("python",
     "front-ir", "tensor-ir") overrides the choice by file name."""
-    return [prog for _, _, prog in load_source_stages(path, enabled, kind)]
+    return [prog for _, _, prog in load_source_stages(path, enabled, kind, cfg)]
 
 
-def load_source_stages(path: str, enabled: Sequence[str] = (), kind: str = "auto"):
+def load_source_stages(path: str, enabled: Sequence[str] = (), kind: str = "auto",
+                       cfg: OptConfig = DEFAULT_CONFIG):
     """As ``load_source_file``, with each program's FrontIR and LoomLambda
     entries: ``(front_ir, loom_lambda, program)``, the first two None for a
     TensorIR source."""
@@ -156,9 +167,9 @@ def load_source_stages(path: str, enabled: Sequence[str] = (), kind: str = "auto
                 "front-ir" if path.endswith(".front_ir.json") else "tensor-ir")
     if kind == "python":
         from .frontend import python_stages
-        return python_stages(path, enabled)
+        return python_stages(path, enabled, cfg)
     if kind == "front-ir":
-        return _front_ir_file_stages(path, enabled)
+        return _front_ir_file_stages(path, enabled, cfg)
     if kind == "tensor-ir":
         return [(None, None, prog) for prog in load_entries_file(path)]
     raise TensorIRError(f"unknown input kind {kind!r} (expected python, front-ir or tensor-ir)")
@@ -166,7 +177,8 @@ def load_source_stages(path: str, enabled: Sequence[str] = (), kind: str = "auto
 
 def discover_entries(project_root: str, module_filters: Sequence[str] = (),
                      entry_filters: Sequence[str] = (), enabled: Sequence[str] = (),
-                     input_kind: str = "auto") -> List[EntryBundle]:
+                     input_kind: str = "auto", cfg: OptConfig = DEFAULT_CONFIG
+                     ) -> List[EntryBundle]:
     """Collect entries of a project (cuda_backend.ml:158-178, 307-326): every
     ``*.tensor_ir.json``, every ``*.front_ir.json`` and every Python module
     with ``@loom.entry`` functions below the root (only the Python modules
@@ -189,7 +201,7 @@ def discover_entries(project_root: str, module_filters: Sequence[str] = (),
         module = module_name_of_file(path)
         if mfilt and module.lower() not in mfilt:
             continue
-        for front, lam, prog in load_source_stages(path, enabled):
+        for front, lam, prog in load_source_stages(path, enabled, cfg=cfg):
             if efilt and prog.entry_name.lower() not in efilt:
                 continue
             bundles.append(EntryBundle(module, path, prog, plan_entry(prog, module, enabled),
@@ -318,7 +330,8 @@ def _report(title, project_root, package, opts, artifact, header, source, bundle
              f"- header: `{header}`",
              f"- source: `{source}`",
              f"- exported entrypoints: `{len(bundles)}`",
-             "- enabled optimizations: " + (", ".join(opts.enabled) if opts.enabled else "none"),
+             "- enabled optimizations: " + (", ".join(in_catalogue_order(opts.enabled))
+                                            if opts.enabled else "none"),
              ""]
     for b in bundles:
         p = b.plan
@@ -404,7 +417,7 @@ def generate_package(project_root: str, out_dir: str, opts: Optional[Options] = 
     project_root = os.path.abspath(project_root)
     package = package_name or package_name_of_root(project_root)
     bundles = discover_entries(project_root, module_filters, entry_filters, opts.enabled,
-                               input_kind)
+                               input_kind, opts.config)
     if not bundles:
         raise TensorIRError("no Loom entries matched the requested project selection")
     symbols = [b.plan.symbol for b in bundles]
@@ -464,7 +477,7 @@ def compile_entry(source_file: str, entry_name: str, out_dir: str,
     FrontIR source."""
     opts = opts or Options()
     module = module_name_of_file(source_file)
-    loaded = load_source_stages(source_file, opts.enabled, input_kind)
+    loaded = load_source_stages(source_file, opts.enabled, input_kind, opts.config)
     stages = [st for st in loaded if st[2].entry_name == entry_name]
     front_ir_file = input_kind == "front-ir" or (
         input_kind == "auto" and source_file.endswith(".front_ir.json"))

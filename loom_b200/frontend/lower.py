@@ -172,13 +172,15 @@ def _norm(e, env):
     raise FrontendError(f"unknown FrontIR node kind {k!r}")
 
 
-def loom_lambda(front: dict, enabled=()) -> dict:
+def loom_lambda(front: dict, enabled=(), cfg=None) -> dict:
     """FrontIR entry -> LoomLambda entry (JSON form of loomLambda.ml:74-137),
     after the scalar passes that `enabled` switches on (normalize.ml:195-258;
     normalize_passes.py)."""
+    from ..optconfig import DEFAULT_CONFIG
     from .normalize_passes import apply_normalize_passes
+    cfg = cfg or DEFAULT_CONFIG
     env = {p["name"]: _Value(_var(p["name"], p["type"])) for p in front["params"]}
-    body = apply_normalize_passes(_norm(front["body"], env), enabled)
+    body = apply_normalize_passes(_norm(front["body"], env), enabled, cfg.small_inline_nodes)
     return {"entry": front["entry"], "params": [dict(p) for p in front["params"]],
             "return_type": front["return_type"], "body": body}
 
@@ -396,10 +398,11 @@ def _use_counts(prog: TI.Program) -> Dict[int, int]:
     return counts
 
 
-def annotate(prog: TI.Program, enabled=()) -> TI.Program:
+def annotate(prog: TI.Program, enabled=(), cfg=None) -> TI.Program:
     """Metrics, reduction shapes and handling hints of every node
     (tensor_passes.ml:513-548); the hints depend on the materialisation flags
     in `enabled`."""
+    from ..optconfig import DEFAULT_CONFIG
     from .passes import materialization_hint
     uses = _use_counts(prog)
     for n in prog.nodes:
@@ -423,11 +426,12 @@ def annotate(prog: TI.Program, enabled=()) -> TI.Program:
                                      else "weighted-mapped" if n.source.scalar_params
                                      else "mapped")
         n.handling_hint = materialization_hint(
-            enabled, n.metrics, None if isinstance(n, TI.Elementwise1D) else n.reduction_shape)
+            enabled, n.metrics, None if isinstance(n, TI.Elementwise1D) else n.reduction_shape,
+            cfg or DEFAULT_CONFIG)
     return prog
 
 
-def tensor_ir(lam: dict, enabled=()) -> TI.Program:
+def tensor_ir(lam: dict, enabled=(), cfg=None) -> TI.Program:
     """LoomLambda entry -> annotated, validated TensorIR program, after the
     restated TensorIR passes that `enabled` switches on (passes.py)."""
     from .passes import apply_tensor_passes
@@ -452,11 +456,16 @@ def tensor_ir(lam: dict, enabled=()) -> TI.Program:
         raise FrontendError("entry lowered to a scalar expression instead of a reduction result")
     prog = TI.Program(entry_name=lam["entry"], params=params, result_kind=kind, result=ref,
                       nodes=tz.nodes)
-    prog = apply_tensor_passes(prog, enabled)
-    annotate(prog, enabled)
+    from ..optconfig import DEFAULT_CONFIG
+    cfg = cfg or DEFAULT_CONFIG
+    prog = apply_tensor_passes(prog, enabled, cfg)
+    annotate(prog, enabled, cfg)
     TI.validate(prog)
     return prog
 
 
-def program_from_front_ir(front: dict, enabled=()) -> TI.Program:
-    return tensor_ir(loom_lambda(front, enabled), enabled)
+def program_from_front_ir(front: dict, enabled=(), cfg=None) -> TI.Program:
+    """FrontIR entry -> TensorIR, with the passes `enabled` switches on and
+    the thresholds of `cfg` (an ``OptConfig``; the reference's defaults when
+    None)."""
+    return tensor_ir(loom_lambda(front, enabled, cfg), enabled, cfg)

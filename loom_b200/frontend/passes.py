@@ -17,7 +17,7 @@ that reaches a backend has producer maps folded into their consumers:
 each gated by the materialisation policy
 (``src/loom_tensorize/materialization_policy.ml:1-94``), and the handling
 hints that annotation attaches (``materialization_hint``, ``:1-44``).  The
-thresholds are the reference's defaults (``configs/optimizations/current.json``).
+thresholds come from the optimisation configuration (``loom_b200/optconfig.py``).
 
 and the body rewrites and node CSE (``:6-60``, ``:337-513``), applied before
 and again after fusion (``:554-666``):
@@ -45,16 +45,11 @@ from typing import Dict, List, Sequence, Tuple
 
 from .. import tensor_ir as TI
 from . import analysis as A
+from ..optconfig import DEFAULT_CONFIG, OptConfig
 from .lower import _use_counts, body_metrics
 
-# configs/optimizations/current.json (the reference's defaults)
-SMALL_CLONE_NODES = 12
-BRANCHY_FUSION_COMPLEXITY = 6
-POINTWISE_MATERIALIZATION_COMPLEXITY = 5
-MATERIALIZE_MULTI_USE_COMPLEXITY = 4
-REDUCTION_BODY_CSE_MIN_OCCURRENCES = 2
-REDUCTION_MATERIALIZE_COMPLEXITY = 5
-REDUCTION_LATE_FUSION_COMPLEXITY = 8
+# The thresholds come from the optimisation configuration (``--opt-config``;
+# by default the values of the reference's configs/optimizations/current.json).
 
 FUSE_FLAGS = ("map-chain-collapse", "elementwise-fusion", "small-producer-clone")
 
@@ -65,43 +60,48 @@ def _on(enabled: Sequence[str], flag: str) -> bool:
 
 # --- materialisation policy (materialization_policy.ml) -----------------------
 
-def allow_inline_producer(enabled, m: TI.BodyMetrics, use_count: int) -> str:
+def allow_inline_producer(enabled, m: TI.BodyMetrics, use_count: int,
+                          cfg: OptConfig = DEFAULT_CONFIG) -> str:
     """"fuse", "clone" or "disallow" for an element-wise producer
     (materialization_policy.ml:46-68)."""
     branch_guard = (_on(enabled, "branch-aware-fusion-guard") and m.has_branch
-                    and m.scalar_complexity >= BRANCHY_FUSION_COMPLEXITY)
+                    and m.scalar_complexity >= cfg.branchy_fusion_complexity_threshold)
     pointwise_guard = (_on(enabled, "pointwise-materialization-guard")
                        and (m.has_branch or m.has_div)
-                       and m.scalar_complexity >= POINTWISE_MATERIALIZATION_COMPLEXITY)
+                       and m.scalar_complexity
+                       >= cfg.pointwise_materialization_complexity_threshold)
     if branch_guard or pointwise_guard:
         return "disallow"
     if use_count <= 1:
         return "fuse"
     if (_on(enabled, "materialization-choice")
-            and m.scalar_complexity >= MATERIALIZE_MULTI_USE_COMPLEXITY):
+            and m.scalar_complexity >= cfg.materialize_multi_use_complexity_threshold):
         return "disallow"
     return "clone"
 
 
 def allow_inline_into_reduction(enabled, m: TI.BodyMetrics, use_count: int,
-                                target_complexity: int) -> str:
+                                target_complexity: int,
+                                cfg: OptConfig = DEFAULT_CONFIG) -> str:
     """The same decision for a producer feeding a reduction
     (materialization_policy.ml:70-94)."""
     late_guard = _on(enabled, "reduction-late-fusion-guard") and (
-        m.scalar_complexity + target_complexity >= REDUCTION_LATE_FUSION_COMPLEXITY
+        m.scalar_complexity + target_complexity >= cfg.reduction_late_fusion_complexity_threshold
         or (m.has_branch and target_complexity > 0)
-        or m.repeated_subexpressions >= REDUCTION_BODY_CSE_MIN_OCCURRENCES)
+        or m.repeated_subexpressions >= cfg.reduction_body_cse_min_occurrences)
     if late_guard:
         return "disallow"
     if (_on(enabled, "reduction-materialization-choice")
-            and (m.scalar_complexity >= REDUCTION_MATERIALIZE_COMPLEXITY or m.has_branch
+            and (m.scalar_complexity >= cfg.reduction_materialize_complexity_threshold
+                 or m.has_branch
                  or m.div_count > 0)
             and use_count > 1):
         return "disallow"
-    return allow_inline_producer(enabled, m, use_count)
+    return allow_inline_producer(enabled, m, use_count, cfg)
 
 
-def materialization_hint(enabled, m: TI.BodyMetrics, reduction_shape) -> str:
+def materialization_hint(enabled, m: TI.BodyMetrics, reduction_shape,
+                         cfg: OptConfig = DEFAULT_CONFIG) -> str:
     """The handling hint annotation attaches to a node
     (materialization_policy.ml:1-44)."""
     if not _on(enabled, "materialization-choice"):
@@ -110,14 +110,15 @@ def materialization_hint(enabled, m: TI.BodyMetrics, reduction_shape) -> str:
         if reduction_shape == "branchy-mapped":
             return "prefer-materialize"
         if reduction_shape == "ratio-mapped" and (
-                m.scalar_complexity >= REDUCTION_MATERIALIZE_COMPLEXITY or m.div_count > 0):
+                m.scalar_complexity >= cfg.reduction_materialize_complexity_threshold
+                or m.div_count > 0):
             return "prefer-materialize"
         if reduction_shape == "weighted-mapped" and (
                 m.repeated_subexpressions > 0 or m.estimated_uses > 1):
             return "prefer-clone"
         if m.estimated_uses <= 1:
             return "prefer-fuse"
-        if (m.scalar_complexity >= REDUCTION_MATERIALIZE_COMPLEXITY
+        if (m.scalar_complexity >= cfg.reduction_materialize_complexity_threshold
                 or m.repeated_subexpressions > 0):
             return "prefer-materialize"
         return "prefer-clone"
@@ -127,9 +128,9 @@ def materialization_hint(enabled, m: TI.BodyMetrics, reduction_shape) -> str:
         return "prefer-materialize"
     if m.estimated_uses <= 1:
         return "prefer-fuse"
-    if m.scalar_complexity <= SMALL_CLONE_NODES:
+    if m.scalar_complexity <= cfg.small_clone_nodes:
         return "prefer-clone"
-    if m.has_branch or m.scalar_complexity >= MATERIALIZE_MULTI_USE_COMPLEXITY:
+    if m.has_branch or m.scalar_complexity >= cfg.materialize_multi_use_complexity_threshold:
         return "prefer-materialize"
     return "prefer-clone"
 
@@ -169,7 +170,7 @@ def _fresh(base: str, suffix: str, existing: Sequence[TI.InputBinding]) -> str:
 # --- the passes -----------------------------------------------------------------
 
 def fuse_program(prog: TI.Program, enabled, allow_clone: bool = False,
-                 clone_limit: int = SMALL_CLONE_NODES) -> TI.Program:
+                 cfg: OptConfig = DEFAULT_CONFIG) -> TI.Program:
     """Element-wise producers into element-wise consumers
     (tensor_passes.ml:130-232)."""
     uses = _use_counts(prog)
@@ -191,10 +192,11 @@ def fuse_program(prog: TI.Program, enabled, allow_clone: bool = False,
                 inputs.append(b)
                 continue
             decision = allow_inline_producer(enabled, body_metrics(use_count, producer.body),
-                                             use_count)
+                                             use_count, cfg)
             if decision == "disallow" or (
                     decision == "clone"
-                    and (not allow_clone or TI.complexity(producer.body) > clone_limit)):
+                    and (not allow_clone
+                         or TI.complexity(producer.body) > cfg.small_clone_nodes)):
                 inputs.append(b)
                 continue
             if use_count == 1:
@@ -217,7 +219,7 @@ def fuse_program(prog: TI.Program, enabled, allow_clone: bool = False,
 
 
 def reduce_map_fusion_program(prog: TI.Program, enabled, allow_clone: bool = False,
-                              clone_limit: int = SMALL_CLONE_NODES) -> TI.Program:
+                              cfg: OptConfig = DEFAULT_CONFIG) -> TI.Program:
     """A reduction over an element-wise node becomes a mapped reduction
     (tensor_passes.ml:251-335)."""
     uses = _use_counts(prog)
@@ -235,10 +237,10 @@ def reduce_map_fusion_program(prog: TI.Program, enabled, allow_clone: bool = Fal
             nodes.append(node)
             continue
         decision = allow_inline_into_reduction(
-            enabled, body_metrics(use_count, producer.body), use_count, 0)
+            enabled, body_metrics(use_count, producer.body), use_count, 0, cfg)
         if decision == "disallow" or (
                 decision == "clone"
-                and (not allow_clone or TI.complexity(producer.body) > clone_limit)):
+                and (not allow_clone or TI.complexity(producer.body) > cfg.small_clone_nodes)):
             nodes.append(node)
             continue
         if use_count == 1:
@@ -349,12 +351,12 @@ def branchy_reduction_rescue(prog: TI.Program) -> TI.Program:
     return prog
 
 
-def reduction_body_cse(prog: TI.Program) -> TI.Program:
-    """Bodies with at least REDUCTION_BODY_CSE_MIN_OCCURRENCES repeated
+def reduction_body_cse(prog: TI.Program, cfg: OptConfig = DEFAULT_CONFIG) -> TI.Program:
+    """Bodies with at least ``reduction_body_cse_min_occurrences`` repeated
     subexpressions (tensor_passes.ml:414-438)."""
     for n in _mapped(prog):
         body = n.source.body
-        if A.repeated_subexpressions(body) >= REDUCTION_BODY_CSE_MIN_OCCURRENCES:
+        if A.repeated_subexpressions(body) >= cfg.reduction_body_cse_min_occurrences:
             _with_mapped(n, body=A.canonicalize(A.simplify(A.reduction_body_cse_expr(body))))
     return prog
 
@@ -413,7 +415,7 @@ TENSOR_BODY_FLAGS = ("tensor-canonicalize", "reduction-input-simplify", "reducti
                      "reduction-body-cse", "tensor-cse")
 
 
-def _body_passes(prog: TI.Program, enabled) -> TI.Program:
+def _body_passes(prog: TI.Program, enabled, cfg: OptConfig) -> TI.Program:
     if _on(enabled, "tensor-canonicalize"):
         prog = canonicalize_program(prog)
     if _on(enabled, "reduction-input-simplify"):
@@ -427,23 +429,24 @@ def _body_passes(prog: TI.Program, enabled) -> TI.Program:
     if _on(enabled, "reduction-body-canonicalize"):
         prog = reduction_body_canonicalize(prog)
     if _on(enabled, "reduction-body-cse"):
-        prog = reduction_body_cse(prog)
+        prog = reduction_body_cse(prog, cfg)
     return prog
 
 
-def apply_tensor_passes(prog: TI.Program, enabled: Sequence[str]) -> TI.Program:
+def apply_tensor_passes(prog: TI.Program, enabled: Sequence[str],
+                        cfg: OptConfig = DEFAULT_CONFIG) -> TI.Program:
     """The restated passes in the reference's order (tensor_passes.ml:554-666):
     the body rewrites, fusion, dead-node removal, node CSE, then the body
     rewrites once more."""
     enabled = tuple(enabled)
-    prog = _body_passes(prog, enabled)
+    prog = _body_passes(prog, enabled, cfg)
     clone = _on(enabled, "small-producer-clone")
     if any(_on(enabled, f) for f in FUSE_FLAGS):
-        prog = fuse_program(prog, enabled, allow_clone=clone)
+        prog = fuse_program(prog, enabled, allow_clone=clone, cfg=cfg)
     if _on(enabled, "reduce-map-fusion"):
-        prog = reduce_map_fusion_program(prog, enabled, allow_clone=clone)
+        prog = reduce_map_fusion_program(prog, enabled, allow_clone=clone, cfg=cfg)
     if _on(enabled, "shape-use-simplify"):
         prog = shape_use_simplify(prog)
     if _on(enabled, "tensor-cse"):
         prog = tensor_cse(prog)
-    return _body_passes(prog, enabled)
+    return _body_passes(prog, enabled, cfg)

@@ -261,3 +261,73 @@ def test_list_entries_and_front_ir_commands(tmp_path):
     bad = _cli("compile", str(fir), "--entry", "relu", "--out", str(tmp_path / "o"))
     assert bad.returncode != 0
     assert "FrontIR entry saxpy does not match requested --entry relu" in bad.stderr
+
+
+CSE_KERNEL = '''import loom
+
+
+@loom.entry
+def twice(x: loom.Tensor1, y: loom.Tensor1) -> float:
+    return loom.Tensor1.reduce_sum(loom.Tensor1.map2(lambda xi, yi: (xi - yi) + (xi - yi), x, y))
+'''
+
+
+def test_flags_are_checked_and_reported_in_catalogue_order(tmp_path):
+    # optimization_config.ml:182-206, :269-274; test/python/test_cli.py:511-540
+    src = tmp_path / "kernels.py"
+    src.write_text(KERNELS)
+    bad = _cli("compile", str(src), "--entry", "saxpy", "--out", str(tmp_path / "b"),
+               "--enable-opt", "no-such-flag")
+    assert bad.returncode != 0
+    assert "unknown optimization flag no-such-flag in --enable-opt" in bad.stderr
+    out = tmp_path / "o"
+    ok = _cli("compile", str(src), "--entry", "saxpy", "--out", str(out), "--emit", "tensor-ir",
+              "--enable-opt", "normalized-dce", "--enable-opt", "scalar-const-fold",
+              "--enable-opt", "tensor-cse", "--disable-opt", "tensor-cse")
+    assert ok.returncode == 0, ok.stderr
+    manifest = json.loads((out / "manifest.json").read_text())
+    assert manifest["optimizations"]["enabled"] == ["scalar-const-fold", "normalized-dce"]
+    assert manifest["optimizations"]["config"]["small_inline_nodes"] == 20
+    assert "enabled optimizations: scalar-const-fold, normalized-dce" in \
+        (out / "report.md").read_text()
+
+
+def test_opt_config_file_steers_the_passes(tmp_path):
+    # optimization_config.ml:85-180: required fields, integers only, the
+    # others defaulting; the thresholds reach the restated passes
+    from loom_b200.optconfig import DEFAULT_CONFIG
+    src = tmp_path / "kernels.py"
+    src.write_text(CSE_KERNEL)
+    cfg = DEFAULT_CONFIG.to_json()
+    del cfg["source_path"]
+    flags = ["--enable-opt", "reduce-map-fusion", "--enable-opt", "reduction-body-cse"]
+
+    def body(config_path=None):
+        out = tmp_path / f"o{len(list(tmp_path.iterdir()))}"
+        extra = ["--opt-config", str(config_path)] if config_path else []
+        r = _cli("compile", str(src), "--entry", "twice", "--out", str(out), "--emit",
+                 "tensor-ir", *flags, *extra)
+        assert r.returncode == 0, r.stderr
+        manifest = json.loads((out / "manifest.json").read_text())
+        return json.loads((out / "tensor_ir.json").read_text()), manifest
+
+    tir, _ = body()
+    red = tir["nodes"][-1]
+    assert red["source"]["body"]["op"] == "add"        # one repeat: below the default of 2
+    cfg["reduction_body_cse_min_occurrences"] = 1
+    path = tmp_path / "cfg.json"
+    path.write_text(json.dumps(cfg))
+    tir, manifest = body(path)
+    body_ = tir["nodes"][-1]["source"]["body"]
+    # x+x -> 2*x, then canonical order ("b:sub:..." < "f:2"): (x - y) * 2
+    assert body_["op"] == "mul" and body_["rhs"] == {"kind": "f32", "value": 2.0}
+    assert body_["lhs"]["op"] == "sub"
+    assert manifest["optimizations"]["config"]["source_path"] == str(path)
+    for broken, message in (({k: v for k, v in cfg.items() if k != "version"},
+                             "missing Loom optimization config field version"),
+                            ({**cfg, "small_inline_nodes": 20.0},
+                             "expected integer field small_inline_nodes")):
+        path.write_text(json.dumps(broken))
+        r = _cli("compile", str(src), "--entry", "twice", "--out", str(tmp_path / "x"),
+                 "--opt-config", str(path))
+        assert r.returncode != 0 and message in r.stderr
