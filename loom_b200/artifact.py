@@ -38,9 +38,9 @@ GENCODE = "arch=compute_100a,code=sm_100a"
 
 # Reference optimisation flags that change this backend's output: the async
 # wrapper return, and the flags that change how map bodies are rendered (and
-# so their bits).  Every other flag is accepted and recorded; the B200 plan
-# (always fused, always vectorised, deterministic reductions) does not depend
-# on it.
+# so their bits).  The front-end pass flags below act before the backend;
+# every other flag is accepted and recorded, as the B200 plan (always fused,
+# always vectorised, deterministic reductions) does not depend on it.
 HONOURED_FLAGS = {"cuda-async-wrapper-return", "cuda-pointwise-tail-tune",
                   "cuda-pointwise-predicated-select", "cuda-pointwise-selected-tail-plan",
                   "cuda-body-trait-analysis", "shared-body-trait-analysis"}
