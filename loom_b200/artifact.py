@@ -419,7 +419,8 @@ def generate_package(project_root: str, out_dir: str, opts: Optional[Options] = 
     bundles = discover_entries(project_root, module_filters, entry_filters, opts.enabled,
                                input_kind, opts.config)
     if not bundles:
-        raise TensorIRError("no Loom entries matched the requested project selection")
+        raise TensorIRError("no Loom entry bindings ([@loom.entry], @loom.entry, or LOOM_ENTRY) "
+                            "matched the requested project selection")  # cuda_backend.ml:2761
     symbols = [b.plan.symbol for b in bundles]
     if len(set(symbols)) != len(symbols):
         raise TensorIRError("duplicate entry symbols in project: " + ", ".join(symbols))

@@ -331,3 +331,27 @@ def test_opt_config_file_steers_the_passes(tmp_path):
         r = _cli("compile", str(src), "--entry", "twice", "--out", str(tmp_path / "x"),
                  "--opt-config", str(path))
         assert r.returncode != 0 and message in r.stderr
+
+
+def test_package_rejects_empty_and_unsupported_projects(tmp_path):
+    # test/python/test_package.py:257-287: a project without entries, and one
+    # whose entry calls an unknown function inside a lambda
+    empty = tmp_path / "empty_project"
+    empty.mkdir()
+    (empty / "helpers.py").write_text("def helper(x):\n    return x + 1.0\n")
+    r = _package("--project", str(empty), "--out", str(tmp_path / "o1"))
+    assert r.returncode != 0 and "[@loom.entry]" in r.stderr
+    bad = tmp_path / "unsupported_project"
+    bad.mkdir()
+    front = {"entry": "bad", "params": [{"name": "x", "type": "tensor1<f32>"}],
+             "return_type": "tensor1<f32>",
+             "body": {"kind": "tensor-prim", "op": "tensor-map", "args": [
+                 {"kind": "lambda", "params": [{"name": "xi", "type": "float"}],
+                  "body": {"kind": "apply",
+                           "fn": {"kind": "var", "name": "bad_scalar", "type": "(float -> float)"},
+                           "args": [{"kind": "var", "name": "xi", "type": "float"}]}},
+                 {"kind": "var", "name": "x", "type": "tensor1<f32>"}]}}
+    (bad / "bad.front_ir.json").write_text(json.dumps(front))
+    r = _package("--project", str(bad), "--out", str(tmp_path / "o2"))
+    assert r.returncode != 0
+    assert "unknown function call inside scalar lambda: bad_scalar" in r.stderr
