@@ -41,9 +41,11 @@ def _options(ns) -> artifact.Options:
     for item in ns.disable_opt or []:
         disabled += [f for f in item.split(",") if f]
     config = load_config(ns.opt_config) if ns.opt_config else DEFAULT_CONFIG
+    platform = "current" if ns.cuda_platform.lower() in ("current", "native") else "generic"
     return artifact.Options(enabled=parse_cli_flags(enabled, disabled),
                             multi_gpu=not ns.no_multi_gpu,
-                            kind=getattr(ns, "kind", "shared"), config=config)
+                            kind=getattr(ns, "kind", "shared"), config=config,
+                            cuda_platform=platform)
 
 
 def _input_kind(value: str) -> str:
@@ -98,9 +100,10 @@ def main(argv=None) -> int:
 
     def common(p):
         p.add_argument("--out", required=True)
-        p.add_argument("--target", default="cuda", choices=["cuda"])
+        # --backend is loomc's alias of --target (src/loom_cli/main.ml:422-424)
+        p.add_argument("--target", "--backend", dest="target", default="cuda")
         p.add_argument("--cuda-arch", default="sm_100a")
-        p.add_argument("--cuda-platform", default="current")
+        p.add_argument("--cuda-platform", default="generic")
         p.add_argument("--opt-config")
         p.add_argument("--enable-opt", action="append")
         p.add_argument("--disable-opt", action="append")
@@ -119,6 +122,8 @@ def main(argv=None) -> int:
     cp.add_argument("--entry", required=True)
     cp.add_argument("--emit", default="all")
     cp.add_argument("--input-kind", default="auto")
+    cp.add_argument("--autotune", action="store_true")
+    cp.add_argument("--autotune-config")
     common(cp)
 
     le = sub.add_parser("list-entries", help="list the entries of a Python source")
@@ -142,6 +147,19 @@ def main(argv=None) -> int:
     if ns.cuda_arch not in ("sm_100a", "sm_100"):
         print(f"error: this backend targets sm_100a only (got {ns.cuda_arch})", file=sys.stderr)
         return 2
+    # the reference's target, platform and autotuning checks (main.ml:392-412,
+    # cuda_backend.ml:69-76)
+    problem = None
+    if ns.target.lower() != "cuda":
+        problem = (f"this backend builds --target cuda only (got {ns.target}); the Triton "
+                   "backend is not part of it")
+    elif ns.cuda_platform.lower() not in ("generic", "portable", "current", "native"):
+        problem = f"unknown CUDA platform {ns.cuda_platform} (expected generic or current)"
+    elif getattr(ns, "autotune", False) or getattr(ns, "autotune_config", None):
+        problem = "The generated CUDA backend does not support Triton autotuning flags"
+    if problem:
+        print(f"error: {problem}", file=sys.stderr)
+        return 1
     try:
         if ns.cmd == "package":
             kind = _input_kind(ns.input_kind)

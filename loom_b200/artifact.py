@@ -79,6 +79,9 @@ class Options:
     # the tuning configuration (``--opt-config``); its pass thresholds steer
     # the front end
     config: OptConfig = DEFAULT_CONFIG
+    # ``--cuda-platform`` as recorded in the manifest; the sm_100a build is the
+    # same for both
+    cuda_platform: str = "generic"
 
     @property
     def async_return(self) -> bool:
@@ -300,9 +303,13 @@ def _manifest(mode, project_root, package, opts, artifact, header, source, entry
         "package_name": package,
         "artifact_kind": opts.kind,
         "cuda_arch": CUDA_ARCH,
-        "cuda_platform": "b200",
-        "cuda_tuning": {"block_size": 256, "unroll_float4": 4, "tile_elements": 4096,
-                        "max_partials": 4096, "grid": "sm_count x resident CTAs per SM"},
+        "cuda_platform": opts.cuda_platform,
+        # the launch constants of loom_b200/csrc/loom_b200_device.cuh
+        "cuda_tuning": {"block_size": 256, "finalize_threads": 1024, "max_partials": 32768,
+                        "max_cluster_ctas": 8,
+                        "map_float4_per_input_per_thread": {"one_input": 2, "more_inputs": 1},
+                        "reduce_float4_per_input_per_thread": {"one_input": 4, "more_inputs": 2},
+                        "grid": "one CTA per tile"},
         "artifact_path": artifact,
         "header_path": header,
         "source_path": source,

@@ -355,3 +355,25 @@ def test_package_rejects_empty_and_unsupported_projects(tmp_path):
     r = _package("--project", str(bad), "--out", str(tmp_path / "o2"))
     assert r.returncode != 0
     assert "unknown function call inside scalar lambda: bad_scalar" in r.stderr
+
+
+def test_compile_target_platform_and_autotune_checks(tmp_path):
+    # test/python/test_cli.py:222-323 (the CUDA-target cases) and main.ml:392-424
+    src = tmp_path / "kernels.py"
+    src.write_text(KERNELS)
+    r = _cli("compile", str(src), "--entry", "relu", "--backend", "cuda", "--out",
+             str(tmp_path / "o"), "--emit", "tensor-ir", "--cuda-platform", "native")
+    assert r.returncode == 0, r.stderr
+    manifest = json.loads((tmp_path / "o" / "manifest.json").read_text())
+    assert manifest["cuda_platform"] == "current"
+    assert manifest["cuda_tuning"]["max_partials"] == 32768
+    r = _cli("compile", str(src), "--entry", "relu", "--target", "cuda", "--out",
+             str(tmp_path / "a"), "--autotune")
+    assert r.returncode != 0
+    assert "does not support Triton autotuning flags" in r.stderr
+    r = _cli("compile", str(src), "--entry", "relu", "--out", str(tmp_path / "p"),
+             "--cuda-platform", "fastest")
+    assert r.returncode != 0 and "unknown CUDA platform fastest" in r.stderr
+    r = _cli("compile", str(src), "--entry", "relu", "--target", "triton", "--out",
+             str(tmp_path / "t"))
+    assert r.returncode != 0 and "--target cuda only" in r.stderr
