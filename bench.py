@@ -901,6 +901,9 @@ def run_workload_sweep(args) -> None:
     CUDA events, 20 calls after 3 warm-up, a write-then-read 512 MiB L2
     flush before each), inputs N(0,1) and the harness's scalar arguments.
     GB/s = 4 bytes x (tensor inputs + 1 for a tensor result) x N / time.
+    --workload-package picks the build: the default flags ("workloads"),
+    the fusion and body-rendering flags ("workloads_flags"), or the flag set
+    of the reference harness's tuned CUDA profile ("workloads_cuda_fixed").
     Prints one JSON line."""
     import torch
     from loom_b200.build import BUILT_DIR
@@ -909,7 +912,7 @@ def run_workload_sweep(args) -> None:
     table_path = os.path.join(ROOT, "tests", "golden", "sources", "workloads", "workloads.json")
     with open(table_path) as fh:
         table = json.load(fh)
-    pkg = Package(os.path.join(BUILT_DIR, "workloads"))
+    pkg = Package(os.path.join(BUILT_DIR, args.workload_package))
     peak, peak_src = read_peak()
     stream = torch.cuda.current_stream()
     flush = (torch.empty(128 << 20, dtype=torch.float32, device="cuda"),
@@ -934,7 +937,7 @@ def run_workload_sweep(args) -> None:
             del kw, out, call
         torch.cuda.empty_cache()
     emit({"mode": "workload_sweep", "metric": METRIC, "unit": "GB/s", "peak": peak,
-          "peak_source": peak_src, "points": points})
+          "peak_source": peak_src, "package": args.workload_package, "points": points})
 
 
 def main():
@@ -961,6 +964,9 @@ def main():
                     help="time each single-entry configuration at its own N instead of the step")
     ap.add_argument("--workload-sweep", action="store_true",
                     help="time the reference harness's 33 kernels at the --sweep sizes")
+    ap.add_argument("--workload-package", default="workloads",
+                    choices=["workloads", "workloads_flags", "workloads_cuda_fixed"],
+                    help="which build of the harness's kernels --workload-sweep times")
     args = ap.parse_args()
     protect_stdout()
     if args.warmup < 3:
