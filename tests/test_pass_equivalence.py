@@ -4,6 +4,9 @@ tests/golden/sources/pass_programs (make_pass_programs.py) is lowered without
 flags and with the pass flags, and both TensorIR programs are evaluated in
 float64 on the same inputs.
 
+The FrontIR the front end prints for these entries equals what the
+reference's own Python frontend printed for them (committed fixture).
+
 The passes re-associate sums and products and fold constants, so the two
 evaluations differ by rounding only (relative 1e-9 of the magnitudes
 involved); an operand swapped in a non-commutative operation, a min turned
@@ -91,6 +94,20 @@ def _inputs(n, seed):
     inp = {t: rng.standard_normal(n) for t in ("x", "y", "w")}
     inp.update(SCALARS)
     return inp
+
+
+def test_front_ir_of_the_pass_programs_matches_the_reference_frontend():
+    # tests/golden/pass_programs_front_ir.json holds what the reference's
+    # Python frontend printed for every entry (make_front_ir.py), so the
+    # programs the passes rewrite start from the reference's own FrontIR
+    import json
+    from loom_b200.frontend import front_ir
+    golden = json.load(open(os.path.join(HERE, "golden", "pass_programs_front_ir.json")))
+    with open(SOURCE, encoding="utf-8") as fh:
+        src = fh.read()
+    assert len(golden) == 40
+    for entry, want in golden.items():
+        assert front_ir(src, entry) == want, entry
 
 
 @pytest.mark.parametrize("flags", [ALL_PASSES, tuple(CUDA_FIXED_FLAGS)],
