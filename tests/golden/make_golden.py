@@ -13,7 +13,9 @@ nothing at test time reads it):
   prints for the suite entries, for ``sources/cases/frontend_cases.py`` and for the
   reference's Python examples and package fixture;
 * ``front_ir_errors.json``: the reference frontend's error message for each
-  entry of ``sources/errors/frontend_errors.py``.
+  entry of ``sources/errors/frontend_errors.py``;
+* ``list_entries.json``: its entry listing (``list-entries-json``) for the
+  suite, the cases and the random pass programs.
 """
 
 import json
@@ -71,6 +73,18 @@ def main(ref: str) -> None:
                          else ""}
     with open(os.path.join(HERE, "front_ir_errors.json"), "w") as fh:
         json.dump(errors, fh, indent=1, sort_keys=True)
+        fh.write("\n")
+    # the frontend's entry listing (list-entries-json) for the Python sources
+    listings = {}
+    for rel in (os.path.join("loom_b200", "suite", "kernels.py"),
+                os.path.join("tests", "golden", "sources", "cases", "frontend_cases.py"),
+                os.path.join("tests", "golden", "sources", "pass_programs", "pass_programs.py")):
+        proc = subprocess.run([sys.executable, frontend, "list-entries-json",
+                               os.path.join(ROOT, rel)], capture_output=True, text=True,
+                              check=True)
+        listings[rel.replace(os.sep, "/")] = json.loads(proc.stdout)
+    with open(os.path.join(HERE, "list_entries.json"), "w") as fh:
+        json.dump(listings, fh, indent=1, sort_keys=True)
         fh.write("\n")
     print("golden fixtures written to", HERE)
 

@@ -121,3 +121,13 @@ def test_package_discovers_python_sources(tmp_path):
         "loom_frontend_cases_" + e["name"] for e in list_entries(_read(CASES_SRC))}
     with pytest.raises(FrontendError):
         discover_entries(os.path.dirname(ERRORS_SRC))
+
+
+def test_entry_listing_matches_reference_frontend():
+    # the reference frontend's list-entries-json output (make_golden.py):
+    # names in its order, parameter names and kinds
+    listings = json.load(open(os.path.join(GOLDEN, "list_entries.json")))
+    assert len(listings) == 3
+    for rel, want in listings.items():
+        path = os.path.join(ROOT, *rel.split("/"))
+        assert list_entries(_read(path), path) == want["entries"], rel
