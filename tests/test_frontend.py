@@ -131,3 +131,17 @@ def test_entry_listing_matches_reference_frontend():
     for rel, want in listings.items():
         path = os.path.join(ROOT, *rel.split("/"))
         assert list_entries(_read(path), path) == want["entries"], rel
+
+
+def test_random_rejected_entries_give_the_reference_messages():
+    # 40 seeded entries with one rejected construct each, at random depths
+    # (sources/errors/make_random_errors.py): the same message, line and
+    # column as the reference's Python frontend
+    errors = json.load(open(os.path.join(GOLDEN, "random_errors.json")))
+    src = _read(os.path.join(GOLDEN, "sources", "errors", "random_errors.py"))
+    assert len(errors) == 40
+    for entry, ref in errors.items():
+        assert ref["returncode"] != 0, entry
+        with pytest.raises(FrontendError) as info:
+            front_ir(src, entry)
+        assert ref["stderr"] == "Python frontend error: " + str(info.value), entry
