@@ -30,6 +30,8 @@ import re
 import shutil
 import subprocess
 
+from pathlib import Path
+
 import numpy as np
 import pytest
 
@@ -99,8 +101,30 @@ def _same_bits(got, ref):
 @pytest.mark.parametrize("project, flags", BUILDS,
                          ids=[f"{p}-{len(f)}flags" for p, f in BUILDS])
 def test_generated_bodies_match_the_oracle_on_the_host(tmp_path, project, flags):
+    check_project(tmp_path, os.path.join(SOURCES, project), flags, project)
+
+
+def test_structured_random_entries_on_the_host(tmp_path):
+    # tests/golden/sources/front_programs without the two entries that the
+    # reference's normalize rejects (tests/test_front_programs.py)
+    src = open(os.path.join(SOURCES, "front_programs", "front_programs.py")).read()
+    for entry in ("f000", "f020"):
+        start = src.index(f"@loom.entry\ndef {entry}(")
+        end = src.find("@loom.entry", start + 1)
+        src = src[:start] + (src[end:] if end >= 0 else "")
+    root = tmp_path / "front_programs"
+    root.mkdir()
+    (root / "front_programs.py").write_text(src)
+    for flags in ((), tuple(CUDA_FIXED_FLAGS)):
+        check_project(tmp_path / f"f{len(flags)}", str(root), flags, "front_programs")
+
+
+def check_project(tmp_path, root, flags, project):
+    """Package `root` with `flags` (sources only), compile its body functors
+    for the host and compare every map's bits, and every reduction's
+    per-element values, with the oracle's."""
     from oracle.loom_oracle import Oracle
-    root = os.path.join(SOURCES, project)
+    os.makedirs(tmp_path, exist_ok=True)
     opts = artifact.Options(enabled=list(flags), multi_gpu=False)
     res = artifact.generate_package(root, str(tmp_path / "pkg"), opts, build=False)
     src = open(res.source_path).read()
@@ -118,7 +142,7 @@ def test_generated_bodies_match_the_oracle_on_the_host(tmp_path, project, flags)
         bodies[sym] = (text, fields, k)
         (maps if b.program.result_kind == "tensor" else reductions).append(b)
     assert maps or reductions
-    lib = _host_library(tmp_path, "bodies", bodies)
+    lib = _host_library(Path(tmp_path), "bodies", bodies)
     # a reduction's body renders with the default rules whatever the flags
     # (the rendering flags select map kernels), so its values are checked
     # against an oracle map built without them
