@@ -38,6 +38,31 @@ SOURCE = os.path.join(PROJECT, "pass_programs.py")
 ALL_PASSES = (NORMALIZE_FLAGS + TENSOR_BODY_FLAGS + FUSE_FLAGS
               + ("reduce-map-fusion", "shape-use-simplify"))
 SCALARS = {"a": 0.75, "b": -1.25}
+# further flag sets of the reference harness's profiles
+# (experiments/source/data/profiles/loom_profiles.json)
+POINTWISE_GUARDED = ("scalar-const-fold", "if-simplify", "arith-reassociate", "branch-hoist",
+                     "lambda-inline-small", "scalar-cse", "normalized-dce", "tensor-canonicalize",
+                     "map-chain-collapse", "elementwise-fusion", "shape-use-simplify", "tensor-cse",
+                     "materialization-choice", "branch-aware-fusion-guard",
+                     "pointwise-materialization-guard", "elementwise-plan-specialize",
+                     "pointwise-shape-plan", "multi-use-fusion-guard", "storage-reuse-pack",
+                     "launch-bucket-specialize")
+REDUCTION_CORE = ("scalar-const-fold", "if-simplify", "arith-reassociate", "lambda-inline-small",
+                  "scalar-cse", "normalized-dce", "tensor-canonicalize", "reduction-input-simplify",
+                  "reduction-body-normalize", "reduction-body-canonicalize",
+                  "reduction-accumulator-shape", "reduction-reuse-hoist", "reduction-body-cse",
+                  "reduce-map-fusion", "map-chain-collapse", "tensor-cse", "shape-use-simplify",
+                  "materialization-choice", "reduction-materialization-choice",
+                  "reduction-plan-specialize", "reduction-classify", "reduction-tree-plan",
+                  "reduction-split-plan", "reduction-small-plan-specialize",
+                  "reduction-stage-sizing", "reduction-stage-balance",
+                  "reduction-partial-shape-pack", "reduction-class-aware-buckets",
+                  "storage-reuse-pack", "launch-bucket-specialize")
+# the late-fusion guard and clone flags, which no profile enables together
+GUARDS = ("reduce-map-fusion", "map-chain-collapse", "small-producer-clone",
+          "reduction-late-fusion-guard", "materialization-choice",
+          "reduction-materialization-choice", "branchy-reduction-rescue", "scalar-hoist",
+          "let-float")
 
 
 def eval_expr(e, env):
@@ -110,8 +135,10 @@ def test_front_ir_of_the_pass_programs_matches_the_reference_frontend():
         assert front_ir(src, entry) == want, entry
 
 
-@pytest.mark.parametrize("flags", [ALL_PASSES, tuple(CUDA_FIXED_FLAGS)],
-                         ids=["all_passes", "cuda_fixed"])
+@pytest.mark.parametrize("flags", [ALL_PASSES, tuple(CUDA_FIXED_FLAGS), POINTWISE_GUARDED,
+                                   REDUCTION_CORE, GUARDS],
+                         ids=["all_passes", "cuda_fixed", "pointwise_guarded", "reduction_core",
+                              "guards"])
 def test_passes_preserve_values(flags):
     plain = {p.entry_name: p for p in python_programs(SOURCE)}
     rewritten = {p.entry_name: p for p in python_programs(SOURCE, flags)}
