@@ -377,3 +377,20 @@ def test_compile_target_platform_and_autotune_checks(tmp_path):
     r = _cli("compile", str(src), "--entry", "relu", "--target", "triton", "--out",
              str(tmp_path / "t"))
     assert r.returncode != 0 and "--target cuda only" in r.stderr
+
+
+def test_compile_tensor_ir_input_has_no_front_end_dumps(tmp_path):
+    # a TensorIR source enters after loomc's front end: no FrontIR or
+    # LoomLambda to dump, and pipeline.json says so with nulls
+    src = os.path.join(ROOT, "oracle", "suite_kernels.tensor_ir.json")
+    out = tmp_path / "tir"
+    r = _cli("compile", src, "--entry", "dot", "--out", str(out), "--emit", "all",
+             "--input-kind", "tensor-ir")
+    assert r.returncode == 0, r.stderr
+    names = {p.name for p in out.iterdir()}
+    assert {"tensor_ir.json", "kernel_plan.json", "cuda_plan.json", "backend_analysis.json",
+            "lambda.sexp", "pipeline.json", "libdot.so"} <= names
+    assert not names & {"front_ir.json", "loom_lambda.json"}
+    pipeline = json.loads((out / "pipeline.json").read_text())
+    assert pipeline["front_ir"] is None and pipeline["loom_lambda"] is None
+    assert pipeline["tensor_ir"]["entry_name"] == "dot"
