@@ -102,6 +102,14 @@ def test_small_producer_clone_duplicates_a_shared_producer():
                                                         "small-producer-clone",
                                                         "shape-use-simplify"))
     assert [n.id for n in dropped.nodes] == [1]
+    # the clone limit is the configuration's small_clone_nodes (tensor_passes.ml:
+    # ~clone_complexity_limit); the producer has complexity 1
+    from dataclasses import replace
+    from loom_b200.optconfig import DEFAULT_CONFIG
+    tight = replace(DEFAULT_CONFIG, small_clone_nodes=0)
+    kept = apply_tensor_passes(copy.deepcopy(prog), ("map-chain-collapse",
+                                                     "small-producer-clone"), tight)
+    assert kept.nodes[1].inputs[0].source == TI.NodeRef(0)
 
 
 @pytest.mark.parametrize("entry", ["dot", "l2_norm_sq", "max_value", "pipeline_sum",
