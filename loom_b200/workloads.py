@@ -83,6 +83,26 @@ def generate(dist: str, n: int, seed: int) -> np.ndarray:
     raise ValueError(f"unknown distribution {dist!r}")
 
 
+def harness_inputs(tensor_inputs, scalar_args, n: int, seed_offset: int = 0) -> Dict[str, object]:
+    """Seeded host inputs for one kernel of the reference harness's table
+    (``experiments/source/data/common/workloads.json``).
+
+    The harness draws every tensor from N(0, 1) with seed ``base + n +
+    seed_offset + k*104729`` for the k-th tensor input and passes the table's
+    scalar arguments as floats (``experiments/source/harness/run.py:941-960``;
+    the ``+ n`` is its ``config["seed"] + size``).  It generates on the GPU
+    with torch; these inputs keep the seeds and the distribution but come
+    from numpy's PCG64 on the host, so the CPU oracle sees the same arrays.
+    """
+    seed = BASE_SEED + n + seed_offset
+    out: Dict[str, object] = {}
+    for k, name in enumerate(tensor_inputs):
+        out[name] = generate("normal", n, seed + k * INPUT_SEED_STRIDE)
+    for name, value in dict(scalar_args).items():
+        out[name] = float(value)
+    return out
+
+
 def entry_inputs(entry: str, n: int, seed_offset: int = 0) -> Dict[str, object]:
     """Seeded host inputs for one suite entry (tensor k gets seed + k*104729)."""
     tensors, scalars, dist = ENTRY_SPECS[entry]
