@@ -29,9 +29,9 @@
 //    for maps and 3-4% for reductions: the static stride leaves the slowest
 //    SMs with the tail.  Map kernels have no loop at all; reductions walk
 //    whole tiles with a grid stride only past kMaxPartials CTAs;
-//  * reductions: sums accumulate each thread's tile chunk in fp32 and fold
-//    the chunk into an fp64 per-thread accumulator; CTAs reduce with
-//    xor-shuffle butterflies and write one fp64 partial each to the caller's
+//  * reductions: sums convert every value to fp64 and accumulate in fp64
+//    (a fixed tree per thread and tile, then a per-thread accumulator);
+//    CTAs reduce with xor-shuffle butterflies and write one fp64 partial each to the caller's
 //    workspace (at most kMaxPartials; past that CTAs take several tiles with
 //    a grid stride); the finalize CTA sums the partials in a fixed order.
 //    No float atomics anywhere: the result is bit-reproducible for a given
@@ -208,15 +208,24 @@ map_scalar_kernel(float* __restrict__ out, const Ptrs<Body::kInputs> in, const i
 // ---------------------------------------------------------------------------
 // reductions
 
+// A reduction op.  Acc is the per-thread and per-CTA accumulator; Chunk is
+// what one thread folds a tile's values into before absorbing them.  Sums
+// convert every fp32 value to fp64 and add in fp64 (pairwise inside a float4,
+// then in a fixed tree over the tile), so the result is the fp64 sum of the
+// fp32 values up to fp64 rounding, whatever the data's cancellation: the
+// fp64 pipe (64 lanes per SM per clock on B200) and the f32->f64 conversions
+// have several times the throughput an HBM-bound stream needs.  Max stays
+// fp32 fmaxf, which is exact in any order.
 struct SumOp {
   using Acc = double;
+  using Chunk = double;
   static __device__ __forceinline__ double init() { return 0.0; }
-  static __device__ __forceinline__ float chunk4(const float4& v) {
-    return __fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w));
+  static __device__ __forceinline__ double chunk4(const float4& v) {
+    return __dadd_rn(__dadd_rn((double)v.x, (double)v.y), __dadd_rn((double)v.z, (double)v.w));
   }
-  static __device__ __forceinline__ float chunk2(float a, float b) { return __fadd_rn(a, b); }
-  static __device__ __forceinline__ double absorb(double acc, float chunk) {
-    return __dadd_rn(acc, (double)chunk);
+  static __device__ __forceinline__ double chunk2(double a, double b) { return __dadd_rn(a, b); }
+  static __device__ __forceinline__ double absorb(double acc, double chunk) {
+    return __dadd_rn(acc, chunk);
   }
   static __device__ __forceinline__ double combine(double a, double b) { return __dadd_rn(a, b); }
   static __device__ __forceinline__ float to_float(double a) { return __double2float_rn(a); }
@@ -224,6 +233,7 @@ struct SumOp {
 
 struct MaxOp {
   using Acc = float;
+  using Chunk = float;
   static __device__ __forceinline__ float init() { return -INFINITY; }
   static __device__ __forceinline__ float chunk4(const float4& v) {
     return fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
@@ -256,7 +266,7 @@ __device__ __forceinline__ typename Op::Acc block_reduce(typename Op::Acc v) {
 
 // Fixed-order fold of the U per-float4 chunks of one tile.
 template <class Op, int U>
-__device__ __forceinline__ float fold_chunks(const float (&c)[U]) {
+__device__ __forceinline__ typename Op::Chunk fold_chunks(const typename Op::Chunk (&c)[U]) {
   if constexpr (U == 1) {
     return c[0];
   } else if constexpr (U == 2) {
@@ -335,7 +345,7 @@ reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInp
     for (int u = 0; u < U; ++u)
 #pragma unroll
       for (int k = 0; k < K; ++k) v[u][k] = load_stream(src[k] + u * kThreads);
-    float c[U];
+    typename Op::Chunk c[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) c[u] = Op::chunk4(apply4(body, v[u]));
     acc = Op::absorb(acc, fold_chunks<Op, U>(c));
@@ -387,7 +397,7 @@ reduce_scalar_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::k
 #pragma unroll
         for (int k = 0; k < Body::kInputs; ++k)
           v[u][k] = load_stream(in.p[k] + t + u * kThreads + threadIdx.x);
-      float c[kU / 4];
+      typename Op::Chunk c[kU / 4];
 #pragma unroll
       for (int q = 0; q < kU / 4; ++q) {
         float4 f;

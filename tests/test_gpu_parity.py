@@ -3,11 +3,13 @@
 Bar (what a result must meet to pass):
   * maps (saxpy, relu, affine_relu) and max_value: bit-exact (NaN only has to
     be NaN);
-  * sums (dot, l2_norm_sq, pipeline_sum): |gpu - ref| <= 1e-6 * max(1, log2 n)
-    * max(|ref|, sqrt(sum v_i^2)), ref = the oracle's fp64 sum of the fp32
-    per-element values v_i.  For random data sqrt(sum v_i^2) is the natural
-    size of the sum, so this is the stated 1e-6*log2(N) relative bound; the
-    second term only matters when the sum cancels far below that size.
+  * sums (dot, l2_norm_sq, pipeline_sum): the relative bound the B200 backend
+    is specified to, |gpu - ref| <= 1e-6 * max(1, log2 n) * |ref|, with ref
+    the oracle's fp64 sum of the fp32 per-element values.  The kernels add
+    every value in fp64, so a sum is within about one fp32 rounding of ref
+    whatever the data's cancellation; the largest relative error seen is
+    recorded, and the last test checks it stays within 2^-23 (one fp32 ulp),
+    far inside the bound.
 """
 
 import math
@@ -34,20 +36,17 @@ def to_device(arr: np.ndarray, offset: int = 0) -> torch.Tensor:
     return view
 
 
-def sum_scale(entry, inp):
-    if entry == "dot":
-        v = inp["x"].astype(np.float64) * inp["y"]
-    elif entry == "l2_norm_sq":
-        v = inp["x"].astype(np.float64) ** 2
-    else:
-        z = np.maximum(0.75 * inp["x"].astype(np.float64) + inp["y"], 0.0)
-        v = z * inp["w"]
-    return math.sqrt(float(np.sum(v * v)))
+# largest |gpu - ref| / |ref| seen by check_sum in this session, per entry
+WORST_REL = {}
 
 
 def check_sum(entry, got, ref, inp, n):
-    tol = 1e-6 * max(1.0, math.log2(n)) * max(abs(ref), sum_scale(entry, inp))
-    assert abs(got - ref) <= tol, (entry, n, got, ref, tol)
+    """north_star's bar for a sum: |got - ref| <= 1e-6 * max(1, log2 n) * |ref|."""
+    err = abs(got - ref)
+    bar = 1e-6 * max(1.0, math.log2(n)) * abs(ref)
+    assert err <= bar, (entry, n, got, ref, bar)
+    rel = err / abs(ref) if ref != 0 else 0.0
+    WORST_REL[entry] = max(WORST_REL.get(entry, 0.0), rel)
 
 
 def run_entry(pkg, entry, inp, offsets=None):
@@ -235,3 +234,12 @@ def test_loader_rejects_bad_outputs_and_mixed_devices(suite_pkg):
     if torch.cuda.device_count() > 1:
         with pytest.raises(ValueError):
             suite_pkg["dot"](x=x, y=torch.zeros(1000, device="cuda:1"))
+
+
+def test_zz_worst_sum_error_is_within_one_fp32_ulp():
+    """The sums checked above (when they ran in this session) all came within
+    2^-23 relative of the fp64 reference: the fp32 rounding of the result."""
+    if not WORST_REL:
+        pytest.skip("no sum was checked in this session")
+    print("largest relative sum error per entry:", WORST_REL)
+    assert max(WORST_REL.values()) <= 2.0 ** -23, WORST_REL
