@@ -146,11 +146,12 @@ def render_header(package: str, plans: List[EntryPlan], multi_gpu: bool = True,
         if plan.program.entry_name in noalloc:
             lines.append(f"/* {plan.symbol}_noalloc: no counterpart in the reference.  The same "
                          "reduction for callers that cannot allocate device memory (no workspace "
-                         "argument): its per-CTA partials live in a static 32 KiB device array "
-                         "(4096 slots) that the library holds on every GPU that loads it; the "
-                         "grid is capped at 4096 CTAs, so any n >= 1 fits.  "
-                         "The first call on a device looks the array up (make it before any "
-                         "stream capture); calls that overlap on the GPU race on the array. */")
+                         f"argument): its per-CTA values live in a static {NOALLOC_BYTES}-byte device "
+                         f"array ({NOALLOC_SLOTS} CTA slots) that the library holds on every GPU "
+                         f"that loads it; the grid is capped at {NOALLOC_SLOTS} CTAs, so any n >= 1 "
+                         "fits.  The first call on a device, and the first after its context is "
+                         "re-created (cudaDeviceReset), looks the array up: make it before any "
+                         "stream capture.  Calls that overlap on the GPU race on the array. */")
             lines.append(noalloc_prototype(plan))
     if multi_gpu:
         lines.append("")
@@ -248,10 +249,8 @@ def render_entry(plan: EntryPlan, async_return: bool, multi_gpu: bool = True,
     if plan.kind == "map":
         L.append("  return loomb::launch_map(out, loom_in, n, loom_body, loom_stream);")
     else:
-        acc = "double" if plan.reduce_kind == "sum" else "float"
-        L.append(f"  {acc}* loom_partials = reinterpret_cast<{acc}*>(loomb::workspace_base(workspace));")
-        L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, loom_partials, "
-                 "loomb::partial_capacity(n), out, nullptr, loom_stream);")
+        L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, "
+                 "loomb::workspace_scratch(workspace, n), out, nullptr, loom_stream);")
     L.append("}")
     L.append("")
     # the reference entry: legacy default stream, synchronous unless built with
@@ -420,79 +419,146 @@ def render_comm_api(package: str) -> str:
     ])
 
 
-def render_noalloc(plan: EntryPlan) -> str:
-    """The no-allocation variant of one reduction entry (see the header
-    comment of ``<sym>_noalloc``)."""
-    if plan.kind != "reduce":
-        raise ValueError(f"{plan.program.entry_name}: only a reduction uses scratch memory")
-    sym = plan.symbol
-    acc = "double" if plan.reduce_kind == "sum" else "float"
-    decls = _param_decls(plan) + ["int64_t n", "float* out", "void* stream"]
-    L = [
+NOALLOC_SLOTS = 4096
+# a 256-byte header and the single-pass fold's view of the slot region (the
+# larger of its two views): 16 bytes per CTA and per group of 256 CTAs
+NOALLOC_BYTES = 256 + 16 * (NOALLOC_SLOTS + NOALLOC_SLOTS // 256)
+
+
+def render_noalloc_scratch() -> str:
+    """The static scratch array shared by every ``<sym>_noalloc`` entry of a
+    package, and the per-context lookup of its device address (emitted once
+    per generated source)."""
+    return "\n".join([
         "// ---------------------------------------------------------------------------",
-        f"// {sym}_noalloc -- {plan.program.entry_name} for callers that cannot allocate.",
+        "// Scratch for the _noalloc entries: callers that cannot allocate.",
         "//",
         "// Some callers have no way to give this library device memory: a host",
         "// application or plugin whose framework owns every byte of the GPU through",
         "// its own allocator, a latency-critical loop where cudaMalloc (which may",
         "// synchronise the whole device) is not allowed, or a C caller of the plain",
         "// ABI, whose reductions otherwise demand a sized workspace argument (only",
-        "// maps have a _noworkspace form).  This entry needs nothing but the inputs",
-        "// and the 1-float output: the per-CTA partials go to the static array",
-        "// below, 4096 fp64 slots (32 KiB), which every GPU that loads the library",
-        "// holds until the process exits.  The entry caps its grid at those 4096",
-        "// CTAs (for large n each CTA then walks several tiles), so every n >= 1",
-        "// fits; while n needs no more than 4096 tiles (2^23 elements for a",
-        "// two-input body) it launches the same grid as the workspace entry and",
-        "// gives the same bits, past that it differs only in rounding order.",
+        "// maps have a _noworkspace form).  A _noalloc entry needs nothing but the",
+        "// inputs and the 1-float output: its per-CTA values go to the static array",
+        f"// below, a 256-byte header and {NOALLOC_SLOTS} CTA slots ({NOALLOC_BYTES} bytes in all),",
+        "// which every GPU that loads the library holds until the process exits.",
         "//",
         "// Host code must not hand the array's name to a kernel: on the host it is",
-        "// only a stand-in for the device symbol.  The entry looks up the real device",
-        "// address with cudaGetSymbolAddress the first time it runs on each device",
-        "// (with that device current) and caches it, so make the first call on each",
-        "// device before any stream capture.  Nothing in the array has to start at",
-        "// zero: every slot the finalize kernel reads was written by the same call's",
-        "// first kernel.  All calls share the array, so two calls whose kernels",
-        "// overlap on the GPU (different streams, no ordering between them) race and",
-        "// corrupt each other's partials: keep calls ordered on one stream.",
-        "constexpr int kLoomNoallocSlots = 4096;",
-        "static __device__ __align__(256) double loom_noalloc_scratch[kLoomNoallocSlots];",
+        "// only a stand-in for the device symbol.  The entries look up the real",
+        "// device address with cudaGetSymbolAddress, with the device current, once",
+        "// per CUDA context: on the first call on each device, and again when that",
+        "// device's context has been re-created since (after cudaDeviceReset the",
+        "// module is loaded anew and the array may move), which the cache notices",
+        "// by the context's unique id.  Make the first call on each device, and",
+        "// the first after a reset, before any stream capture.",
+        f"constexpr int kLoomNoallocSlots = {NOALLOC_SLOTS};",
+        "constexpr size_t kLoomNoallocBytes =",
+        "    loomb::kHeaderBytes + loomb::slot_region_bytes(kLoomNoallocSlots);",
+        f"static_assert(kLoomNoallocBytes == {NOALLOC_BYTES}, \"the documented size\");",
+        "static __device__ __align__(256) unsigned char loom_noalloc_scratch[kLoomNoallocBytes];",
         "",
         "namespace {",
-        "std::mutex loom_noalloc_mutex;",
-        "std::atomic<void*> loom_noalloc_address[loomb::kMaxDevices];",
+        "using LoomCtxGetCurrent = CUresult (*)(CUcontext*);",
+        "using LoomCtxGetId = CUresult (*)(CUcontext, unsigned long long*);",
         "",
-        "// Device address of loom_noalloc_scratch on device `dev` (the current one).",
+        "struct LoomNoallocCache {",
+        "  unsigned long long context_id;",
+        "  void* address;",
+        "};",
+        "",
+        "std::mutex loom_noalloc_mutex;",
+        "LoomNoallocCache loom_noalloc_cache[loomb::kMaxDevices];",
+        "LoomCtxGetCurrent loom_ctx_get_current = nullptr;",
+        "LoomCtxGetId loom_ctx_get_id = nullptr;",
+        "",
+        "// Unique id of the calling thread's current CUDA context (0 when there is",
+        "// none yet); the two driver functions are resolved through the runtime,",
+        "// so the library does not link the driver library itself.  Called with",
+        "// loom_noalloc_mutex held.",
+        "bool loom_current_context_id(unsigned long long* id) {",
+        "  if (loom_ctx_get_current == nullptr || loom_ctx_get_id == nullptr) {",
+        "    void* get_current = nullptr;",
+        "    void* get_id = nullptr;",
+        "    cudaDriverEntryPointQueryResult q1, q2;",
+        "    if (cudaGetDriverEntryPointByVersion(\"cuCtxGetCurrent\", &get_current, 12000,",
+        "                                         cudaEnableDefault, &q1) != cudaSuccess ||",
+        "        cudaGetDriverEntryPointByVersion(\"cuCtxGetId\", &get_id, 12000, cudaEnableDefault,",
+        "                                         &q2) != cudaSuccess ||",
+        "        q1 != cudaDriverEntryPointSuccess || q2 != cudaDriverEntryPointSuccess ||",
+        "        get_current == nullptr || get_id == nullptr) {",
+        "      cudaGetLastError();",
+        "      return false;",
+        "    }",
+        "    loom_ctx_get_current = reinterpret_cast<LoomCtxGetCurrent>(get_current);",
+        "    loom_ctx_get_id = reinterpret_cast<LoomCtxGetId>(get_id);",
+        "  }",
+        "  CUcontext ctx = nullptr;",
+        "  if (loom_ctx_get_current(&ctx) != CUDA_SUCCESS) return false;",
+        "  *id = 0;",
+        "  return ctx == nullptr || loom_ctx_get_id(ctx, id) == CUDA_SUCCESS;",
+        "}",
+        "",
+        "// Device address of loom_noalloc_scratch on device `dev` (the current one)",
+        "// in its current context: looked up on the first call in each context.",
         "int loom_noalloc_scratch_on(int dev, void** address) {",
         "  if (dev < 0 || dev >= loomb::kMaxDevices) return LOOM_STATUS_CUDA_ERROR;",
-        "  void* p = loom_noalloc_address[dev].load(std::memory_order_acquire);",
-        "  if (p == nullptr) {",
-        "    std::lock_guard<std::mutex> lock(loom_noalloc_mutex);",
-        "    p = loom_noalloc_address[dev].load(std::memory_order_relaxed);",
-        "    if (p == nullptr) {",
-        "      const cudaError_t err = cudaGetSymbolAddress(&p, loom_noalloc_scratch);",
-        "      if (err != cudaSuccess || p == nullptr) {",
-        "        cudaGetLastError();",
-        "        return LOOM_STATUS_CUDA_ERROR;",
-        "      }",
-        "      loom_noalloc_address[dev].store(p, std::memory_order_release);",
-        "    }",
+        "  std::lock_guard<std::mutex> lock(loom_noalloc_mutex);",
+        "  unsigned long long id = 0;",
+        "  if (!loom_current_context_id(&id)) return LOOM_STATUS_CUDA_ERROR;",
+        "  LoomNoallocCache& c = loom_noalloc_cache[dev];",
+        "  if (id != 0 && c.address != nullptr && c.context_id == id) {",
+        "    *address = c.address;",
+        "    return LOOM_STATUS_OK;",
         "  }",
+        "  // set-up in this context (cudaGetSymbolAddress also creates the device's",
+        "  // primary context when the thread has none yet)",
+        "  void* p = nullptr;",
+        "  const cudaError_t err = cudaGetSymbolAddress(&p, loom_noalloc_scratch);",
+        "  if (err != cudaSuccess || p == nullptr) {",
+        "    cudaGetLastError();",
+        "    return LOOM_STATUS_CUDA_ERROR;",
+        "  }",
+        "  if (id == 0 && !loom_current_context_id(&id)) return LOOM_STATUS_CUDA_ERROR;",
+        "  c.context_id = id;",
+        "  c.address = p;",
         "  *address = p;",
         "  return LOOM_STATUS_OK;",
         "}",
         "}  // namespace",
         "",
+    ])
+
+
+def render_noalloc(plan: EntryPlan) -> str:
+    """The no-allocation variant of one reduction entry, over the shared
+    scratch of ``render_noalloc_scratch``."""
+    if plan.kind != "reduce":
+        raise ValueError(f"{plan.program.entry_name}: only a reduction uses scratch memory")
+    sym = plan.symbol
+    decls = _param_decls(plan) + ["int64_t n", "float* out", "void* stream"]
+    L = [
+        f"// {sym}_noalloc -- {plan.program.entry_name} with its CTA values in the shared",
+        "// static scratch above (no workspace argument).  The grid is capped at the",
+        f"// {NOALLOC_SLOTS} slots (for large n each CTA then walks several tiles), so every",
+        "// n >= 1 fits; while n needs no more tiles than that, it launches the same",
+        "// grid as the workspace entry and gives the same bits, past that it differs",
+        "// only in rounding order.  Nothing in the array has to start at zero: the",
+        "// fold reads only slots that the same call wrote (each slot carries a",
+        "// check word tied to the call).  All calls of all _noalloc entries share",
+        "// the array, so two calls whose kernels overlap on the GPU (different",
+        "// streams, no ordering between them) race and corrupt each other's",
+        "// values: keep calls ordered on one stream.",
         f'extern "C" int {sym}_noalloc({", ".join(decls)}) {{',
     ]
     L += _validation(plan)
-    L.append(f"  const int64_t loom_slots = (int64_t)(sizeof(loom_noalloc_scratch) / sizeof({acc}));")
     L.append("  void* loom_scratch = nullptr;")
     L.append("  const int loom_status = loom_noalloc_scratch_on(loomb::current_device(), &loom_scratch);")
     L.append("  if (loom_status != LOOM_STATUS_OK) return loom_status;")
     L += _body_setup(plan)
-    L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, static_cast<{acc}*>(loom_scratch), "
-             "loom_slots, out, nullptr, static_cast<cudaStream_t>(stream));")
+    L.append("  const loomb::ReduceScratch loom_rs{static_cast<unsigned char*>(loom_scratch), "
+             "kLoomNoallocSlots};")
+    L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, loom_rs, out, nullptr, "
+             "static_cast<cudaStream_t>(stream));")
     L += ["}", ""]
     return "\n".join(L)
 
@@ -512,7 +578,7 @@ def render_source(package: str, header_include: str, plans: List[EntryPlan],
         '#include "loom_b200_launch.cuh"',
     ]
     if noalloc:
-        parts += ["#include <atomic>", "#include <mutex>"]
+        parts += ["#include <cuda.h>", "#include <mutex>"]
     if multi_gpu:
         parts.append('#include "loom_b200_comm.cuh"')
     parts += ["", "namespace {", ""]
@@ -521,9 +587,11 @@ def render_source(package: str, header_include: str, plans: List[EntryPlan],
     parts += ["}  // namespace", ""]
     for plan in plans:
         parts.append(render_entry(plan, async_return, multi_gpu, package))
-    for plan in plans:
-        if plan.program.entry_name in noalloc:
-            parts.append(render_noalloc(plan))
+    noalloc_plans = [p for p in plans if p.program.entry_name in noalloc]
+    if noalloc_plans:
+        parts.append(render_noalloc_scratch())
+    for plan in noalloc_plans:
+        parts.append(render_noalloc(plan))
     if multi_gpu:
         parts.append(render_comm_api(package))
     return "\n".join(parts)

@@ -1,0 +1,152 @@
+"""The single-pass reduction: a grid of more than 8 CTAs that folds its
+CTAs' values itself (fold_in_last_cta in loom_b200_device.cuh): groups of
+256 consecutive CTAs, whose last CTA folds the group, and the grid's last
+CTA, which folds the group totals.
+
+The CTAs leave their values in slots of the caller's workspace, each with a
+check word tied to the workspace's epoch (the number of folds made on it),
+and nothing zeroes the workspace.  These tests check, against the CPU
+oracle (max bit-exact, sums within 1e-6 * max(1, log2 n) * |ref|):
+
+* grid sizes around the fold's boundaries: 9 CTAs (the smallest fold),
+  256 and 257 (one group, then two), 4097, and 32768 and more tiles (the
+  grid's cap, where CTAs take several tiles), aligned and with a 3-element
+  head;
+* a workspace reused by calls of different sizes, whose older slots must
+  not pass for the current call's;
+* workspaces filled beforehand with zeros, ones, 0xff bytes and random
+  bytes;
+* the epoch, which every fold advances by one, and an epoch wound back;
+* determinism: the same inputs give the same bits.
+"""
+
+import ctypes
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from loom_b200 import workloads
+from test_gpu_parity import check_sum, to_device
+
+pytestmark = pytest.mark.gpu
+
+
+def tile_of(entry):
+    return 4096 if entry in ("l2_norm_sq", "max_value") else 2048
+
+
+def check(entry, got, ref, inp, n):
+    if entry == "max_value":
+        assert got == float(np.float32(ref)), (entry, n, got, ref)
+    else:
+        check_sum(entry, got, ref, inp, n)
+
+
+def call_with_workspace(pkg, entry, dev, ws):
+    """The synchronous reference entry through the C ABI with the caller's
+    workspace `ws` (a uint8 device tensor)."""
+    e = pkg[entry]
+    out = torch.full((1,), float("nan"), device="cuda")
+    args = []
+    for p in e.params:
+        v = dev[p["name"]]
+        args.append(ctypes.c_float(v) if p["kind"] == "scalar-f32"
+                    else ctypes.c_void_p(v.data_ptr()))
+    n = next(v.shape[0] for v in dev.values() if isinstance(v, torch.Tensor))
+    st = e.call_raw(*args, ctypes.c_int64(n), ctypes.c_void_p(out.data_ptr()),
+                    ctypes.c_void_p(ws.data_ptr()), ctypes.c_size_t(ws.numel()))
+    assert st == 0, (entry, n, st)
+    return float(out.cpu()[0])
+
+
+@pytest.mark.parametrize("entry", ["dot", "l2_norm_sq", "max_value", "pipeline_sum"])
+def test_sizes_around_the_fold_boundaries(suite_pkg, oracle, entry):
+    tile = tile_of(entry)
+    sizes = [(9, 0), (9, 5), (255, 1), (256, 0), (256, 1), (257, 0), (4097, 3)]
+    if entry in ("dot", "l2_norm_sq"):
+        sizes += [(32768, 0), (32769, 0), (3 * 32768 + 5, 7)]
+    for g, d in sizes:
+        n = g * tile + d
+        for offset in (0, 3):
+            inp = workloads.entry_inputs(entry, n, seed_offset=g + d + offset)
+            ref = oracle.run(entry, inp)
+            dev = {k: (to_device(v, offset) if isinstance(v, np.ndarray) else v)
+                   for k, v in inp.items()}
+            got = float(suite_pkg[entry](**dev).cpu()[0])
+            check(entry, got, ref, inp, n)
+
+
+def _workspace(pkg, entry, n, fill):
+    size = pkg[entry].workspace_size(n)
+    ws = torch.empty(size, dtype=torch.uint8, device="cuda")
+    if fill == "zeros":
+        ws.zero_()
+    elif fill == "ones":
+        ws.fill_(1)
+    elif fill == "ff":
+        ws.fill_(255)
+    elif fill == "random":
+        g = torch.Generator(device="cuda")
+        g.manual_seed(12345)
+        ws.copy_(torch.randint(0, 256, (size,), dtype=torch.uint8, device="cuda", generator=g))
+    return ws
+
+
+@pytest.mark.parametrize("fill", ["zeros", "ones", "ff", "random"])
+def test_any_prior_workspace_contents(suite_pkg, oracle, fill):
+    n = 1000 * 2048 + 7            # 1001 tiles of a two-input reduction: four groups
+    inp = workloads.entry_inputs("dot", n, seed_offset=77)
+    ref = oracle.run("dot", inp)
+    dev = {k: to_device(v) for k, v in inp.items()}
+    ws = _workspace(suite_pkg, "dot", n, fill)
+    for _ in range(3):
+        check("dot", call_with_workspace(suite_pkg, "dot", dev, ws), ref, inp, n)
+
+
+def test_reused_workspace_with_stale_slots(suite_pkg, oracle):
+    # one workspace, calls that alternate between grids and entries: each call
+    # must read only the slots it wrote, never a slot left by an earlier call
+    big = 4096 * 2048 - 5
+    ws = _workspace(suite_pkg, "dot", big, "random")
+    cases = []
+    for k, n in enumerate([big, 300 * 2048, 9 * 2048 + 1, 4000 * 2048, 17 * 2048]):
+        entry = "dot" if k % 2 == 0 else "pipeline_sum"
+        inp = workloads.entry_inputs(entry, n, seed_offset=500 + k)
+        cases.append((entry, n, inp, oracle.run(entry, inp),
+                      {kk: (to_device(v) if isinstance(v, np.ndarray) else v)
+                       for kk, v in inp.items()}))
+    for _ in range(2):
+        for entry, n, inp, ref, dev in cases:
+            assert suite_pkg[entry].workspace_size(n) <= ws.numel()
+            check(entry, call_with_workspace(suite_pkg, entry, dev, ws), ref, inp, n)
+
+
+def test_epoch_advances_once_per_fold(suite_pkg):
+    n = 600 * 2048
+    inp = workloads.entry_inputs("dot", n, seed_offset=3)
+    dev = {k: to_device(v) for k, v in inp.items()}
+    ws = _workspace(suite_pkg, "dot", n, "zeros")
+    base = (-ws.data_ptr()) % 256            # the header starts at the first 256-byte boundary
+    header = ws[base:base + 8]
+    first = call_with_workspace(suite_pkg, "dot", dev, ws)
+    e1 = int(header.view(torch.int64).item())
+    for _ in range(4):
+        assert call_with_workspace(suite_pkg, "dot", dev, ws) == first
+    assert int(header.view(torch.int64).item()) == e1 + 4
+    # wound back: the next call checks for epoch e1, whose slots later calls
+    # overwrote with other check words, so it must wait for its own values
+    header.view(torch.int64).fill_(e1 - 1)
+    assert call_with_workspace(suite_pkg, "dot", dev, ws) == first
+
+
+def test_fold_is_deterministic(suite_pkg):
+    for entry, n in (("dot", 2047 * 2048 + 3), ("l2_norm_sq", 1500 * 4096 + 1),
+                     ("pipeline_sum", 3000 * 2048)):
+        inp = workloads.entry_inputs(entry, n, seed_offset=11)
+        dev = {k: (to_device(v, 1) if isinstance(v, np.ndarray) else v) for k, v in inp.items()}
+        a = suite_pkg[entry](**dev).cpu().numpy()
+        b = suite_pkg[entry](**dev).cpu().numpy()
+        assert a.view(np.uint32)[0] == b.view(np.uint32)[0]
+        assert not math.isnan(float(a[0]))
