@@ -24,8 +24,19 @@ and "cuda" (its full CUDA set: fused, float4 maps, atomic-output sums).
 
 `--impl reference` times the reference's CPU semantics for the same workload
 on this machine's host cores (the C oracle: the reference has no CPU
-implementation of this path and its OCaml compiler cannot be built here),
-on a bounded sample of N per step.
+implementation of this path and its OCaml compiler cannot be built here):
+each step is one GPU's workload, the seven entries at the same N, and the
+line carries the same `config`.
+
+After the timed region the line's `check` holds the results of the last
+step against independent references (sums against fp64 sums all-reduced
+over the ranks, max exactly, every rank's reductions bit-identical, a window
+of every map bit for bit); a failed check exits non-zero.  Across GPUs
+`exchange_wait` reports how long each reduction's peer exchange waited.
+
+Other modes: `--strong` (fixed global sizes sharded over the ranks),
+`--single ENTRY` (one entry, for profiler captures), `--pipeline-sweep`,
+`--config-sweep`, `--workload-sweep`.
 """
 
 from __future__ import annotations
@@ -242,6 +253,44 @@ def make_inputs(n: int, rank: int):
     return data
 
 
+def suite_config(world: int, n_log2: int) -> dict:
+    """The workload both arms report: the seven suite entries over N = 2^n_log2
+    fp32 elements per GPU."""
+    n = 1 << n_log2
+    return {
+        "workload": ("b200_suite step: saxpy, relu, dot, l2_norm_sq, max_value, "
+                     "affine_relu, pipeline_sum, each over N=2^%d fp32 per GPU" % n_log2),
+        "n_per_gpu": n,
+        "global_n": n * world,
+        "entries": ENTRIES,
+        "l2": "no flush: every input is %d MiB per GPU (> 126 MB L2)" % (4 * n >> 20),
+        "parallelism": f"shard{world} (maps: no communication; reductions: one "
+                       "scalar exchange per call)",
+    }
+
+
+def cpu_suite_inputs(n: int):
+    """loom_b200.workloads.entry_inputs(e, n) for every suite entry, with the
+    arrays shared between entries that draw the same distribution from the
+    same seed (the uniform x, y, w of saxpy, dot, affine_relu and
+    pipeline_sum; the outlier vector of l2_norm_sq and max_value): five
+    arrays of n floats instead of twelve."""
+    from loom_b200 import workloads
+    cache, out = {}, {}
+    for e in ENTRIES:
+        tensors, scalars, dist = workloads.ENTRY_SPECS[e]
+        inp = {}
+        for k, name in enumerate(tensors):
+            key = (dist, k)
+            if key not in cache:
+                cache[key] = workloads.generate(
+                    dist, n, workloads.BASE_SEED + k * workloads.INPUT_SEED_STRIDE)
+            inp[name] = cache[key]
+        inp.update(dict(scalars))
+        out[e] = inp
+    return out
+
+
 def launches_per_call(entry: str, world: int, n: int, peer: bool = True) -> int:
     """Kernels of this library one call launches on n elements per GPU (all
     inputs 16-byte aligned): one for a map, and one for a reduction (a single
@@ -257,6 +306,106 @@ def launches_per_call(entry: str, world: int, n: int, peer: bool = True) -> int:
         per_tile = 256 * 4 * (4 if len(TENSORS[entry]) == 1 else 2)
         return 1 if -(-n // per_tile) > 8 else 2
     return 1 + (1 if entry != "max_value" else 0)
+
+
+def fmaf_f32(a: float, x, y):
+    """Correctly rounded float32 fma(a, x, y) of float32 numpy arrays,
+    computed exactly on the host: a*x is exact in float64 (two 24-bit
+    significands), s = fl64(a*x + y) comes with its exact error e (Knuth's
+    TwoSum), and s rounds to float32 correctly unless it lies exactly
+    halfway between two float32 values, where the sign of e decides."""
+    import numpy as np
+    p = np.float64(np.float32(a)) * x.astype(np.float64)
+    yd = y.astype(np.float64)
+    s = p + yd
+    bb = s - p
+    e = (p - (s - bb)) + (yd - bb)
+    r = s.astype(np.float32)
+    rd = r.astype(np.float64)
+    other = np.where(rd < s, np.nextafter(r, np.float32(np.inf)),
+                     np.nextafter(r, np.float32(-np.inf)))
+    tie = (rd != s) & ((rd + other.astype(np.float64)) * 0.5 == s) & (e != 0)
+    hi, lo = np.maximum(r, other), np.minimum(r, other)
+    return np.where(tie & (e > 0), hi, np.where(tie & (e < 0), lo, r))
+
+
+REDUCTIONS = ["dot", "l2_norm_sq", "max_value", "pipeline_sum"]
+CHECK_SLICE = 1 << 16
+
+
+def _sum_values(entry: str, data, lo: int, hi: int):
+    """The fp32 per-element values a suite sum folds, for [lo, hi) of this
+    rank's inputs (pipeline_sum's fmaf is formed in fp64 and rounded once
+    more to fp32; a double rounding there moves a value by one fp32 ulp at
+    most, far below the sum's bar)."""
+    if entry == "dot":
+        return data["u0"][lo:hi] * data["u1"][lo:hi]
+    if entry == "l2_norm_sq":
+        v = data["outl"][lo:hi]
+        return v * v
+    z = (0.75 * data["u0"][lo:hi].double() + data["u1"][lo:hi].double()).float()
+    return z.clamp_min(0.0) * data["u2"][lo:hi]
+
+
+def check_results(data, outs, n: int, world: int, rank: int):
+    """After the timed region: the results of the last step against
+    independent references.  Sums: the ranks' fp64 sums of the fp32
+    per-element values, all-reduced, with the bar |got - ref| <= 1e-6 *
+    log2(N) * |ref| over the global N; max: exact against a MAX all-reduce
+    of torch.max; every rank's reduction outputs bit-identical to rank 0's;
+    maps: a 2^16-element window of every rank's outputs bit for bit against
+    the host (fmaf formed exactly, relu as x > 0 ? x : 0)."""
+    import numpy as np
+    import torch
+    local = torch.zeros(3, dtype=torch.float64, device="cuda")
+    chunk = 1 << 26
+    for i, e in enumerate(["dot", "l2_norm_sq", "pipeline_sum"]):
+        for lo in range(0, n, chunk):
+            local[i] += _sum_values(e, data, lo, min(n, lo + chunk)).double().sum()
+    mx = data["outl"].max().reshape(1)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(local, op=dist.ReduceOp.SUM)
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    refs = local.tolist()
+    got = {e: float(outs[e][0].item()) for e in REDUCTIONS}
+    bits = {e: int(outs[e].view(torch.int32)[0].item()) for e in REDUCTIONS}
+    all_bits = gather_obj(world, bits)
+    identical = all(b == all_bits[0] for b in all_bits)
+    n_global = n * world
+    bar = 1e-6 * max(1.0, math.log2(n_global))
+    result = {"ranks": world, "global_n": n_global,
+              "reductions_identical_on_every_rank": identical}
+    ok = identical
+    for e, ref in zip(["dot", "l2_norm_sq", "pipeline_sum"], refs):
+        rel = abs(got[e] - ref) / abs(ref) if ref != 0 else abs(got[e])
+        passed = rel <= bar
+        ok &= passed
+        result[e] = {"got": got[e], "ref_fp64": ref, "rel_err": rel, "bar": bar,
+                     "passed": passed}
+    max_ok = got["max_value"] == float(mx.item())
+    ok &= max_ok
+    result["max_value"] = {"got": got["max_value"], "ref": float(mx.item()), "passed": max_ok}
+    L = min(n, CHECK_SLICE)
+    lo = (rank * 7919 * 4096) % max(1, n - L + 1)
+    x = data["u0"][lo:lo + L].cpu().numpy()
+    y = data["u1"][lo:lo + L].cpu().numpy()
+    r = data["nrm"][lo:lo + L].cpu().numpy()
+    want = {"saxpy": fmaf_f32(2.5, x, y),
+            "relu": np.where(r > 0, r, np.float32(0.0)).astype(np.float32)}
+    z = fmaf_f32(0.75, x, y)
+    want["affine_relu"] = np.where(z > 0, z, np.float32(0.0)).astype(np.float32)
+    maps_ok = {}
+    for e, w in want.items():
+        g = outs[e][lo:lo + L].cpu().numpy()
+        maps_ok[e] = bool(np.array_equal(g.view(np.uint32), w.view(np.uint32)))
+    all_maps = gather_obj(world, maps_ok)
+    maps = {e: all(m[e] for m in all_maps) for e in want}
+    ok &= all(maps.values())
+    result["maps_bit_exact"] = maps
+    result["map_elems_checked_per_rank"] = L
+    result["passed"] = bool(ok)
+    return result
 
 
 def run_ours(args) -> None:
@@ -327,6 +476,8 @@ def run_ours(args) -> None:
                    for _ in calls] for _ in range(args.steps)]
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    if comm is not None:
+        comm.exchange_stats(reset=True)
     barrier(world)
     torch.cuda.synchronize()
     sampler.mark_start()
@@ -338,6 +489,7 @@ def run_ours(args) -> None:
     sampler.mark_end()
     barrier(world)
     clocks = sampler.stop()
+    wait = comm.exchange_stats() if comm is not None else None
     elapsed_ms = start.elapsed_time(end)
     kernel_ms = {e: sum(per_kernel[s][i][0].elapsed_time(per_kernel[s][i][1])
                         for s in range(args.steps)) / args.steps
@@ -354,8 +506,10 @@ def run_ours(args) -> None:
     ref_kernels = None
     if world == 1 and args.ref_kernel_steps > 0:
         ref_kernels = run_reference_kernels(data, outs, n, args)
+    check = check_results(data, outs, n, world, rank)
     all_clocks = gather_obj(world, clocks)
     all_kernels = gather_obj(world, kernel_ms)
+    all_wait = gather_obj(world, wait)
 
     if rank == 0:
         traffic = read_traffic()
@@ -385,20 +539,10 @@ def run_ours(args) -> None:
             "dtype": "f32",
             "data": "synthetic (seeded U(-1,1), N(0,1), N(0,1) with 1% x1e3 outliers)",
             "pct_of_peak": round(100 * value / (peak * world), 2),
-            "config": {
-                "workload": ("b200_suite step: saxpy, relu, dot, l2_norm_sq, max_value, "
-                             "affine_relu, pipeline_sum, each over N=2^%d fp32 per GPU"
-                             % args.n_log2),
-                "n_per_gpu": n,
-                "global_n": n * world,
-                "entries": ENTRIES,
-                "l2": "no flush: every input is 1 GiB per GPU (> 126 MB L2)",
-                "parallelism": f"shard{world} (maps: no communication; reductions: one "
-                               "scalar exchange per call)",
-                "exchange": (None if comm is None else
-                             ("peer memory (NVLink P2P stores)" if comm.peer_exchange
-                              else "NCCL all-gather / all-reduce")),
-            },
+            "config": suite_config(world, args.n_log2),
+            "exchange": (None if comm is None else
+                         ("peer memory (NVLink P2P stores)" if comm.peer_exchange
+                          else "NCCL all-gather / all-reduce")),
             "kernels": kernels,
             "roofline": {
                 "bound": "hbm",
@@ -421,7 +565,18 @@ def run_ours(args) -> None:
                 launches_per_call(e, world, n, comm is not None and comm.peer_exchange)
                 for e in ENTRIES),
             "e2e": e2e,
+            "check": check,
         }
+        if comm is not None and comm.peer_exchange:
+            line["exchange_wait"] = {
+                "what": "per rank, over the timed steps: time from sending its value to "
+                        "holding every rank's, in each reduction's peer exchange "
+                        "(%globaltimer stamps in the exchange)",
+                "exchanges_per_rank": all_wait[0]["exchanges"],
+                "mean_us_per_exchange": [round(w["total_us"] / max(1, w["exchanges"]), 2)
+                                         for w in all_wait],
+                "max_us": [round(w["max_us"], 2) for w in all_wait],
+            }
         if ref_kernels is not None:
             ref_kernels["product_over_profile"] = {
                 p: round(value / v["value"], 3) for p, v in ref_kernels["profiles"].items()}
@@ -435,6 +590,8 @@ def run_ours(args) -> None:
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+    if not check["passed"]:
+        sys.exit(1)
 
 
 def run_e2e(pkg, data, outs, n, args, world, comm):
@@ -592,17 +749,17 @@ def run_reference_kernels(data, outs, n, args):
     return result
 
 
-def cpu_baseline(log2n: int, seconds: float, threads: int = 0):
+def cpu_baseline(log2n: int, seconds: float, threads: int = 0, single_log2n: int = 24):
     """The C oracle (the reference's per-element semantics, OpenMP) on the
-    host cores, on N=2^log2n per entry; reports effective GB/s."""
-    import numpy as np
-    from loom_b200 import workloads
+    host cores, on the GPU arm's per-GPU workload (N=2^log2n per entry) for
+    about `seconds`; reports effective GB/s.  The one-core figure is taken on
+    N=2^single_log2n per entry, to keep it to a few seconds."""
     from oracle.loom_oracle import Oracle, load_programs
     threads = threads or len(os.sched_getaffinity(0))
     oracle = Oracle(load_programs(os.path.join(ROOT, "oracle",
                                                "suite_kernels.tensor_ir.json")), name="b200_suite")
     n = 1 << log2n
-    inputs = {e: workloads.entry_inputs(e, n) for e in ENTRIES}
+    inputs = cpu_suite_inputs(n)
     for e in ENTRIES:
         oracle.run(e, inputs[e], threads=threads)
     reps, total = 0, 0.0
@@ -615,37 +772,49 @@ def cpu_baseline(log2n: int, seconds: float, threads: int = 0):
         if total >= seconds:
             break
     step_bytes = sum(bytes_per_elem(e) for e in ENTRIES) * n
-    # the same sample on one core, for about a quarter of the time
+    del inputs
+    n1 = 1 << single_log2n
+    inputs1 = cpu_suite_inputs(n1)
     reps1 = 0
     t0 = time.perf_counter()
     while True:
         for e in ENTRIES:
-            oracle.run(e, inputs[e], threads=1)
+            oracle.run(e, inputs1[e], threads=1)
         reps1 += 1
         total1 = time.perf_counter() - t0
         if total1 >= seconds / 4:
             break
+    step_bytes1 = sum(bytes_per_elem(e) for e in ENTRIES) * n1
     return {"value": round(step_bytes * reps / total / 1e9, 2), "unit": "GB/s",
             "cores": threads, "kind": "port",
-            "sample": f"the 7 suite entries at N=2^{log2n} each, {reps} steps in {total:.1f} s",
+            "sample": f"the 7 suite entries at N=2^{log2n} each (the GPU arm's per-GPU "
+                      f"workload), {reps} steps in {total:.1f} s",
             "seconds": round(total, 2),
-            "single_thread": {"value": round(step_bytes * reps1 / total1 / 1e9, 2),
+            "single_thread": {"value": round(step_bytes1 * reps1 / total1 / 1e9, 2),
                               "unit": "GB/s", "cores": 1,
-                              "sample": f"{reps1} steps in {total1:.1f} s"}}
+                              "sample": f"N=2^{single_log2n} per entry, {reps1} steps in "
+                                        f"{total1:.1f} s"}}
 
 
 def run_reference(args) -> None:
+    """The reference arm: the CPU restatement of the reference's semantics for
+    this path (the C oracle; the reference has no CPU implementation of it
+    and its OCaml compiler cannot be built here) on all host cores, timing
+    exactly --steps steps after --warmup.  A step is the GPU arm's per-GPU
+    workload, the seven entries at N=2^--n-log2 each; with N GPUs the GPU
+    arm's step is N such shards, which the host cores would process one
+    after another at the same rate, so the line reports the same metric on
+    the GPU arm's config.  Under torchrun only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    # time exactly --steps steps of the bounded sample after --warmup
-    from loom_b200 import workloads
     from oracle.loom_oracle import Oracle, load_programs
     threads = len(os.sched_getaffinity(0))
     oracle = Oracle(load_programs(os.path.join(ROOT, "oracle",
                                                "suite_kernels.tensor_ir.json")), name="b200_suite")
-    n = 1 << args.cpu_log2
-    inputs = {e: workloads.entry_inputs(e, n) for e in ENTRIES}
+    n = 1 << args.n_log2
+    inputs = cpu_suite_inputs(n)
     for _ in range(args.warmup):
         for e in ENTRIES:
             oracle.run(e, inputs[e], threads=threads)
@@ -656,12 +825,14 @@ def run_reference(args) -> None:
     total = time.perf_counter() - t0
     step_bytes = sum(bytes_per_elem(e) for e in ENTRIES) * n
     value = step_bytes * args.steps / total / 1e9
+    sample = (f"one GPU's shard of the workload per step: the 7 suite entries at "
+              f"N=2^{args.n_log2} each" + (f" (of {world} shards)" if world > 1 else ""))
     emit({
         "impl": "reference",
         "metric": METRIC,
         "value": round(value, 2),
         "unit": "GB/s",
-        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+        "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 3),
@@ -670,13 +841,9 @@ def run_reference(args) -> None:
         "vs_baseline": None,
         "dtype": "f32",
         "data": "synthetic (seeded U(-1,1), N(0,1), N(0,1) with 1% x1e3 outliers)",
-        "config": {"workload": ("b200_suite step: saxpy, relu, dot, l2_norm_sq, max_value, "
-                                "affine_relu, pipeline_sum on the host cores, bounded sample "
-                                "N=2^%d per entry (GPU arm: N=2^28 per GPU)" % args.cpu_log2),
-                   "n_per_step": n, "entries": ENTRIES},
+        "config": suite_config(world, args.n_log2),
         "cpu_baseline": {"value": round(value, 2), "unit": "GB/s", "cores": threads,
-                         "kind": "port",
-                         "sample": f"the 7 suite entries at N=2^{args.cpu_log2} each per step"},
+                         "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 2), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     })
@@ -937,6 +1104,238 @@ def run_workload_sweep(args) -> None:
           "peak_source": peak_src, "package": args.workload_package, "points": points})
 
 
+# Fixed global sizes for the strong-scaling mode: (config, entries, log2 of the
+# global N, input distribution); the pipeline at every --strong-sizes size.
+STRONG_L2_MAX = ("l2_norm_sq_max", ("l2_norm_sq", "max_value"), 30, "normal_outliers")
+
+
+def global_slice(kind: str, seed: int, start: int, stop: int, chunk: int = 1 << 24):
+    """Elements [start, stop) of a seeded global input that does not depend
+    on how it is sharded: the global array is cut into fixed chunks, each
+    drawn on the device from its own seed, and a rank draws only the chunks
+    its shard overlaps."""
+    import torch
+    out = torch.empty(stop - start, device="cuda")
+    gen = torch.Generator(device="cuda")
+    c = start // chunk
+    while c * chunk < stop:
+        lo = c * chunk
+        gen.manual_seed(seed * 1000003 + c)
+        if kind == "uniform":
+            v = torch.rand(chunk, device="cuda", generator=gen).mul_(2.0).sub_(1.0)
+        else:
+            v = torch.randn(chunk, device="cuda", generator=gen)
+            v[torch.rand(chunk, device="cuda", generator=gen) < 0.01] *= 1e3
+        s0, s1 = max(start, lo), min(stop, lo + chunk)
+        out[s0 - start:s1 - start] = v[s0 - lo:s1 - lo]
+        c += 1
+    return out
+
+
+def _bound_entry(pkg, entry, tensors, n_local, out, world, comm, stream):
+    """A pre-converted call of `entry` on this rank's shard: the `_dist`
+    entry across GPUs, the stream entry on one."""
+    import ctypes
+    ent = pkg[entry]
+    args_c = []
+    for p in ent.params:
+        if p["kind"] == "scalar-f32":
+            args_c.append(ctypes.c_float(SCALARS[entry][p["name"]]))
+        else:
+            args_c.append(ctypes.c_void_p(tensors[p["name"]].data_ptr()))
+    ws = ent.workspace(max(1, n_local), dist=world > 1)
+    tail = [ctypes.c_int64(n_local), ctypes.c_void_p(out.data_ptr()),
+            ctypes.c_void_p(ws.data_ptr()) if ws is not None else None,
+            ctypes.c_size_t(ws.numel() if ws is not None else 0)]
+    if world > 1:
+        fn, tail = ent.dist_fn, tail + [ctypes.c_void_p(comm.handle)]
+    else:
+        fn = ent.stream_fn
+    tail.append(ctypes.c_void_p(stream.cuda_stream))
+
+    def call():
+        st = fn(*args_c, *tail)
+        if st != 0:
+            raise RuntimeError(f"{entry} returned status {st}")
+    return call, ws
+
+
+def run_strong(args) -> None:
+    """Strong scaling: fixed global sizes sharded over the N ranks with
+    loom_b200.shard (l2_norm_sq and max_value at N = 2^30; the fused
+    pipeline, affine_relu and pipeline_sum, at every --strong-sizes size).
+    Per call: a write-then-read 512 MiB L2 flush, then CUDA events around
+    the call on every rank; a call's time is the max over ranks, and the
+    point's time the median over the calls.  For reductions across GPUs the
+    peer exchange's wait (from sending this rank's value to holding every
+    rank's) is read from the exchange buffer's statistics.  Each point's
+    results are checked: sums against the ranks' fp64 sums of the fp32
+    values (bar 1e-6 * log2(N) * |ref|), max exactly, maps bit for bit on a
+    2^16 window per rank.  Prints one JSON line."""
+    import numpy as np
+    import torch
+    from loom_b200.build import load_suite
+    from loom_b200.shard import shard_bounds
+    world, rank, local = setup_dist(args)
+    pkg = load_suite()
+    comm = pkg.comm_from_process_group() if world > 1 else None
+    stream = torch.cuda.current_stream()
+    peak, peak_src = read_peak()
+    flush = (torch.empty(128 << 20, dtype=torch.float32, device="cuda"),
+             torch.ones(128 << 20, dtype=torch.float32, device="cuda"))
+    configs = [STRONG_L2_MAX] + [("pipeline", ("affine_relu", "pipeline_sum"), k, "uniform")
+                                 for k in args.strong_sizes]
+    points = []
+    all_ok = True
+    for name, entries, log2n, kind in configs:
+        n = 1 << log2n
+        start, stop = shard_bounds(n, world)[rank]
+        n_local = stop - start
+        names = ("x",) if kind != "uniform" else ("x", "y", "w")
+        tens = {t: global_slice(kind, 20260417 + 104729 * k + log2n, start, stop)
+                for k, t in enumerate(names)}
+        reps = 50 if n <= (1 << 26) else (10 if n <= (1 << 30) else 5)
+        for entry in entries:
+            is_map = entry in MAP_ENTRIES
+            out = torch.empty(max(1, n_local) if is_map else 1, device="cuda")
+            call, ws = _bound_entry(pkg, entry, tens, n_local, out, world, comm, stream)
+            for _ in range(3):
+                call()
+            torch.cuda.synchronize()
+            if comm is not None:
+                comm.exchange_stats(reset=True)
+            barrier(world)
+            times = []
+            for _ in range(reps):
+                flush[0].fill_(1.0)
+                flush[1].sum()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                call()
+                b.record(stream)
+                b.synchronize()
+                times.append(a.elapsed_time(b) * 1e3)
+            wait = comm.exchange_stats() if comm is not None else None
+            all_times = gather_obj(world, times)
+            per_call = [max(t[i] for t in all_times) for i in range(reps)]
+            us = statistics.median(per_call)
+            if is_map:
+                L = min(n_local, CHECK_SLICE)
+                lo = (rank * 7919 * 4096) % max(1, n_local - L + 1)
+                x = tens["x"][lo:lo + L].cpu().numpy()
+                y = tens["y"][lo:lo + L].cpu().numpy()
+                z = fmaf_f32(0.75, x, y)
+                want = np.where(z > 0, z, np.float32(0.0)).astype(np.float32)
+                got = out[lo:lo + L].cpu().numpy()
+                ok = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+                ok = all(gather_obj(world, ok))
+                detail = {"maps_bit_exact": ok}
+            else:
+                got = float(out[0].item())
+                if entry == "max_value":
+                    ref = tens["x"].max().reshape(1)
+                    if world > 1:
+                        import torch.distributed as dist
+                        dist.all_reduce(ref, op=dist.ReduceOp.MAX)
+                    ok = got == float(ref.item())
+                    detail = {"got": got, "ref": float(ref.item())}
+                else:
+                    acc = torch.zeros(1, dtype=torch.float64, device="cuda")
+                    for lo in range(0, n_local, 1 << 26):
+                        hi = min(n_local, lo + (1 << 26))
+                        if entry == "l2_norm_sq":
+                            v = tens["x"][lo:hi] * tens["x"][lo:hi]
+                        else:
+                            zz = (0.75 * tens["x"][lo:hi].double()
+                                  + tens["y"][lo:hi].double()).float()
+                            v = zz.clamp_min(0.0) * tens["w"][lo:hi]
+                        acc += v.double().sum()
+                    if world > 1:
+                        import torch.distributed as dist
+                        dist.all_reduce(acc, op=dist.ReduceOp.SUM)
+                    ref = float(acc.item())
+                    rel = abs(got - ref) / abs(ref)
+                    ok = rel <= 1e-6 * max(1.0, math.log2(n))
+                    detail = {"got": got, "ref_fp64": ref, "rel_err": rel}
+                bits = gather_obj(world, float(np.float32(got)))
+                ok = bool(ok) and all(b == bits[0] for b in bits)
+            all_ok &= bool(ok)
+            nbytes = bytes_per_elem(entry) * n
+            row = {"config": name, "entry": entry, "global_n": n, "log2n": log2n,
+                   "n_per_rank_max": max(b - a for a, b in shard_bounds(n, world)),
+                   "us_per_call": round(us, 2), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+                   "frac_of_world_peak": round(nbytes / (us * 1e-6) / 1e9 / (peak * world), 4),
+                   "reps": reps, "check": dict(detail, passed=bool(ok))}
+            if wait is not None and not is_map:
+                waits = gather_obj(world, wait)
+                row["exchange_wait_us_mean"] = [round(w["total_us"] / max(1, w["exchanges"]), 2)
+                                                for w in waits]
+                row["exchange_wait_us_max"] = [round(w["max_us"], 2) for w in waits]
+            points.append(row)
+            del out, ws, call
+        del tens
+        torch.cuda.empty_cache()
+    if rank == 0:
+        emit({"mode": "strong", "metric": METRIC, "unit": "GB/s", "n_gpus": world,
+              "scaling": "strong", "peak": peak, "peak_source": peak_src,
+              "exchange": (None if comm is None else
+                           ("peer memory (NVLink P2P stores)" if comm.peer_exchange
+                            else "NCCL all-gather / all-reduce")),
+              "config": {"workload": "fixed global N sharded over the ranks: l2_norm_sq and "
+                                     "max_value at 2^30 (N(0,1), 1% x1e3 outliers); "
+                                     "affine_relu and pipeline_sum at 2^%s (U(-1,1))"
+                                     % ", 2^".join(str(k) for k in args.strong_sizes),
+                         "l2": "write-then-read 512 MiB flush before every timed call"},
+              "checks_passed": bool(all_ok), "points": points})
+    if comm is not None:
+        comm.check()
+        comm.destroy()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if not all_ok:
+        sys.exit(1)
+
+
+def run_single(args) -> None:
+    """One suite entry at N=2^--n-log2 on one GPU, --steps bound calls after
+    --warmup on the suite's seeded inputs: the small, bounded command that
+    an ncu capture of one kernel runs.  Prints one JSON line with the median
+    device time per call (CUDA events; no L2 flush)."""
+    import torch
+    from loom_b200.build import load_suite
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    pkg = load_suite()
+    entry = args.single
+    n = 1 << args.n_log2
+    data = make_inputs(n, 0)
+    kw = {p: data[t] for p, t in zip(PARAM_NAMES[entry], TENSORS[entry])}
+    kw.update(SCALARS.get(entry, {}))
+    for k in list(data):
+        if k not in TENSORS[entry]:
+            del data[k]
+    out = torch.empty(n if entry in MAP_ENTRIES else 1, device="cuda")
+    stream = torch.cuda.current_stream()
+    call, _ = pkg[entry].bind(out=out, stream=stream, **kw)
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        call()
+        b.record(stream)
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    us = statistics.median(times)
+    emit({"mode": "single", "entry": entry, "n": n, "calls": args.steps,
+          "us_per_call": round(us, 2),
+          "gbs": round(bytes_per_elem(entry) * n / (us * 1e-6) / 1e9, 1)})
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -952,13 +1351,21 @@ def main():
                          "(where every GPU reaches the others) or NCCL")
     ap.add_argument("--ref-kernel-steps", type=int, default=30,
                     help="steps of the reference-style GPU kernels (1 GPU; 0 skips them)")
-    ap.add_argument("--cpu-log2", type=int, default=24)
+    ap.add_argument("--cpu-log2", type=int, default=28,
+                    help="N=2^k per entry of the CPU baseline's sample (default: the GPU "
+                         "arm's per-GPU N)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--pipeline-sweep", action="store_true",
                     help="time the fused pipeline over --sweep sizes instead of the suite step")
     ap.add_argument("--sweep", type=int, nargs="*", default=[10, 14, 18, 22, 26, 30, 32])
     ap.add_argument("--config-sweep", action="store_true",
                     help="time each single-entry configuration at its own N instead of the step")
+    ap.add_argument("--single", choices=ENTRIES,
+                    help="time one entry at N=2^--n-log2 (--steps calls after --warmup)")
+    ap.add_argument("--strong", action="store_true",
+                    help="strong scaling: fixed global sizes sharded over the ranks")
+    ap.add_argument("--strong-sizes", type=int, nargs="*", default=[18, 22, 26, 30, 32],
+                    help="log2 of the pipeline's global N in --strong mode")
     ap.add_argument("--workload-sweep", action="store_true",
                     help="time the reference harness's 33 kernels at the --sweep sizes")
     ap.add_argument("--workload-package", default="workloads",
@@ -968,6 +1375,12 @@ def main():
     protect_stdout()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.single:
+        run_single(args)
+        return
+    if args.strong:
+        run_strong(args)
+        return
     if args.config_sweep:
         run_config_sweep(args)
         return

@@ -120,6 +120,7 @@ def comm_prototypes(package: str) -> List[str]:
         f"int {p}_set_timeout_ms(void* comm, int64_t ms);",
         f"int {p}_peer_exchange(void* comm);",
         f"int {p}_check(void* comm);",
+        f"int {p}_exchange_stats(void* comm, uint64_t* out, int reset);",
     ]
 
 
@@ -159,7 +160,9 @@ def render_header(package: str, plans: List[EntryPlan], multi_gpu: bool = True,
                      "no multi-GPU path): NCCL, plus a peer-memory scalar exchange where every GPU "
                      "reaches the others'. _set_peer_exchange switches paths (every rank alike); "
                      "an exchange waits at most _set_timeout_ms (30 s by default) for the other "
-                     "ranks; _check reports one that gave up. */")
+                     "ranks; _check reports one that gave up; _exchange_stats reads (and with "
+                     "reset zeroes) the total and largest time this rank's exchanges waited, in ns, "
+                     "and their number. */")
         lines += comm_prototypes(package)
     lines += ["", "#ifdef __cplusplus", "}", "#endif", ""]
     return "\n".join(lines)
@@ -415,6 +418,9 @@ def render_comm_api(package: str) -> str:
         "}",
         f'extern "C" int {p}_peer_exchange(void* comm) {{ return loomb::comm_peer_exchange(comm); }}',
         f'extern "C" int {p}_check(void* comm) {{ return loomb::comm_check(comm); }}',
+        f'extern "C" int {p}_exchange_stats(void* comm, uint64_t* out, int reset) {{',
+        "  return loomb::comm_exchange_stats(comm, reinterpret_cast<unsigned long long*>(out), reset);",
+        "}",
         "",
     ])
 

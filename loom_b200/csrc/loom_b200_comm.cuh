@@ -48,6 +48,9 @@ struct PeerTable {
 // Layout of an exchange buffer (kExchangeBytes, zeroed at creation):
 //   +0   u64  exchanges this rank has made (its epoch counter)
 //   +8   u32  status: 0 ok, 1 a wait for a peer ran out
+//   +16  u64  wait statistics of this rank's exchanges: total ns spent from
+//   +24  u64  sending its value to holding every rank's (%globaltimer), the
+//   +32  u64  largest such wait, and the number of exchanges timed
 //   +64  ExchangeSlot[2][kMaxRanks]: the value each rank sent for the
 //        exchanges of even / odd epoch.  Two sets suffice: a rank can be at
 //        most one exchange ahead of any other, since it cannot finish an
@@ -318,6 +321,26 @@ inline int comm_check(void* comm) {
   return status == 0 ? LOOM_STATUS_OK : LOOM_STATUS_COMM_ERROR;
 }
 
+// Copies this rank's exchange wait statistics (total ns, largest ns, number
+// of exchanges timed, since the communicator was created or the last reset)
+// to `out` after waiting for the rank's device, then zeroes them if `reset`.
+// All zero on the NCCL path.
+inline int comm_exchange_stats(void* comm, unsigned long long* out, int reset) {
+  if (comm == nullptr || out == nullptr) return LOOM_STATUS_INVALID_ARGUMENT;
+  Comm* c = static_cast<Comm*>(comm);
+  out[0] = out[1] = out[2] = 0;
+  if (c->xbuf == nullptr) return LOOM_STATUS_OK;
+  DeviceGuard guard;
+  constexpr size_t kBytes = 3 * sizeof(unsigned long long);
+  if (cudaSetDevice(c->device) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(out, c->xbuf + 16, kBytes, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return LOOM_STATUS_CUDA_ERROR;
+  if (reset && (cudaMemset(c->xbuf + 16, 0, kBytes) != cudaSuccess ||
+                cudaDeviceSynchronize() != cudaSuccess))
+    return LOOM_STATUS_CUDA_ERROR;
+  return LOOM_STATUS_OK;
+}
+
 inline int nccl_group_start() { return ncclGroupStart() == ncclSuccess ? 0 : 1; }
 inline int nccl_group_end() { return ncclGroupEnd() == ncclSuccess ? 0 : 1; }
 
@@ -460,6 +483,8 @@ __device__ __forceinline__ void exchange_and_fold(const typename Op::Acc local,
   using Acc = typename Op::Acc;
   unsigned long long* counter = reinterpret_cast<unsigned long long*>(a.own);
   unsigned int* status = reinterpret_cast<unsigned int*>(a.own + 8);
+  unsigned long long* wait_stats = reinterpret_cast<unsigned long long*>(a.own + 16);
+  const unsigned long long t_send = global_ns();
   const unsigned long long epoch = *counter + 1;
   *counter = epoch;
   const int set = (int)(epoch & 1ull) * kMaxRanks;
@@ -487,6 +512,10 @@ __device__ __forceinline__ void exchange_and_fold(const typename Op::Acc local,
     total = Op::combine(total, bits_acc<Acc>(ld_relaxed_sys(&mine[r].bits)));
   }
   a.out[0] = Op::to_float(total);
+  const unsigned long long waited = global_ns() - t_send;
+  wait_stats[0] += waited;
+  if (waited > wait_stats[1]) wait_stats[1] = waited;
+  wait_stats[2] += 1;
 }
 
 // The multi-GPU finish of a single-pass reduction (thread 0 of the grid's

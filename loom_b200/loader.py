@@ -401,6 +401,20 @@ class Comm:
         if st != 0:
             raise LoomError(f"loom_{self.package.name}_comm_check", st)
 
+    def exchange_stats(self, reset: bool = False) -> dict:
+        """This rank's peer-exchange wait statistics since the communicator
+        was created or last reset (after waiting for its device): total and
+        largest time from sending its value to holding every rank's, in
+        microseconds, and the number of exchanges timed; zeroed afterwards
+        with `reset`.  All zero on the NCCL path."""
+        out = (ctypes.c_uint64 * 3)()
+        if self.package._comm_exchange_stats is None:
+            raise RuntimeError(f"{self.package.name} was built without exchange statistics")
+        st = self.package._comm_exchange_stats(ctypes.c_void_p(self.handle), out, int(reset))
+        if st != 0:
+            raise LoomError(f"loom_{self.package.name}_comm_exchange_stats", st)
+        return {"total_us": out[0] / 1e3, "max_us": out[1] / 1e3, "exchanges": int(out[2])}
+
     def destroy(self) -> None:
         if self.handle:
             self.package._comm_destroy(ctypes.c_void_p(self.handle))
@@ -445,6 +459,12 @@ class Package:
             self._comm_peer_exchange.argtypes = [ctypes.c_void_p]
             self._comm_check = getattr(self.lib, prefix + "_check")
             self._comm_check.argtypes = [ctypes.c_void_p]
+            # packages built before the exchange statistics lack the symbol
+            self._comm_exchange_stats = getattr(self.lib, prefix + "_exchange_stats", None)
+            if self._comm_exchange_stats is not None:
+                self._comm_exchange_stats.argtypes = [ctypes.c_void_p,
+                                                      ctypes.POINTER(ctypes.c_uint64),
+                                                      ctypes.c_int]
 
     def __getitem__(self, entry: str) -> Entry:
         return self.entries[entry]

@@ -28,7 +28,7 @@ def _run(args, env=None, timeout=600):
 
 
 def test_reference_arm_prints_one_json_line():
-    proc = _run(["--impl", "reference", "--steps", "2", "--warmup", "3", "--cpu-log2", "12"])
+    proc = _run(["--impl", "reference", "--steps", "2", "--warmup", "3", "--n-log2", "12"])
     assert proc.returncode == 0, proc.stderr
     lines = [line for line in proc.stdout.splitlines() if line.strip()]
     assert len(lines) == 1
@@ -40,11 +40,12 @@ def test_reference_arm_prints_one_json_line():
     assert d["cpu_baseline"]["kind"] == "port"
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
-    assert "workload" in d["config"]
+    # the same workload description as the GPU arm's line
+    assert d["config"] == bench.suite_config(1, 12)
 
 
 def test_reference_arm_other_ranks_print_nothing():
-    proc = _run(["--impl", "reference", "--steps", "1", "--warmup", "3", "--cpu-log2", "10"],
+    proc = _run(["--impl", "reference", "--steps", "1", "--warmup", "3", "--n-log2", "10"],
                 env={"RANK": "1", "WORLD_SIZE": "2"})
     assert proc.returncode == 0, proc.stderr
     assert proc.stdout.strip() == ""
@@ -67,6 +68,50 @@ def test_launch_counts():
     assert all(bench.launches_per_call(e, 4, n, peer=True) == 1 for e in bench.ENTRIES)
     assert [bench.launches_per_call(e, 4, 4096, peer=True) for e in bench.ENTRIES] == \
         [1, 1, 2, 2, 2, 1, 2]
+
+
+def test_fmaf_f32_is_correctly_rounded():
+    # against exact rational arithmetic, on random operands and on operands
+    # built so that a*x + y falls next to the midpoint of two float32 values
+    from fractions import Fraction
+
+    import numpy as np
+
+    def round32(q):
+        f = np.float32(float(q))
+        cands = [f, np.nextafter(f, np.float32(np.inf)), np.nextafter(f, np.float32(-np.inf))]
+        return min(cands, key=lambda c: (abs(Fraction(float(c)) - q),
+                                         int(np.array(c).view(np.uint32)) & 1))
+
+    rng = np.random.default_rng(5)
+    x = list(rng.uniform(-1, 1, 300).astype(np.float32))
+    y = list(rng.uniform(-1, 1, 300).astype(np.float32))
+    for k in range(1, 60):
+        for sh in (24, 25, 26):
+            x.append(np.float32(1 + k * 2.0 ** -23))
+            y.append(np.float32(3 * 2.0 ** -sh) * (1 if k % 2 else -1))
+    x, y = np.array(x, np.float32), np.array(y, np.float32)
+    for a in (2.5, 0.75, 1.0, 3.0):
+        got = bench.fmaf_f32(a, x, y)
+        for i in range(len(x)):
+            q = Fraction(float(np.float32(a))) * Fraction(float(x[i])) + Fraction(float(y[i]))
+            want = round32(q)
+            assert np.array(got[i]).view(np.uint32) == np.array(want).view(np.uint32), (a, i)
+
+
+def test_cpu_inputs_are_the_entries_inputs():
+    import numpy as np
+
+    from loom_b200 import workloads
+    shared = bench.cpu_suite_inputs(1000)
+    for e in bench.ENTRIES:
+        want = workloads.entry_inputs(e, 1000)
+        assert set(shared[e]) == set(want)
+        for k, v in want.items():
+            if isinstance(v, np.ndarray):
+                assert np.array_equal(shared[e][k], v), (e, k)
+            else:
+                assert shared[e][k] == v
 
 
 class _FakeProc:
@@ -108,6 +153,8 @@ def test_product_arm_prints_one_json_line():
                                         for e in bench.ENTRIES)
     assert {"value", "unit", "h2d_bytes_per_step", "d2h_bytes_per_step"} <= set(d["e2e"])
     assert d["e2e"]["h2d_bytes_per_step"] > 0
+    assert d["check"]["passed"], d["check"]
+    assert d["config"] == bench.suite_config(1, 20)
     for profile in ("none", "cuda"):
         ref = d["reference_kernels"]["profiles"][profile]
         assert all(ref["agrees_with_product"].values()), (profile, ref["agrees_with_product"])
