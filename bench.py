@@ -292,20 +292,23 @@ def cpu_suite_inputs(n: int):
 
 
 def launches_per_call(entry: str, world: int, n: int, peer: bool = True) -> int:
-    """Kernels of this library one call launches on n elements per GPU (all
-    inputs 16-byte aligned): one for a map, and one for a reduction (a single
-    CTA, one cluster of up to 8, or a grid that folds its CTAs' values
-    itself).  Across GPUs through peer memory a grid of more than 8 CTAs
-    also exchanges inside that kernel; after a one-CTA or one-cluster grid
-    the exchange is a kernel of its own.  Through NCCL the sums add the rank
-    fold (NCCL's own kernels are not counted).  A tile is 256 threads x 4
-    float4 for one input, x 2 float4 for more."""
-    if entry in MAP_ENTRIES or world == 1:
+    """Kernels of this library one call launches on n elements per GPU: one
+    for a map; for a reduction one when its grid is a single CTA or one
+    cluster (at most 8 tiles of 256 threads x 4 float4 for one input, x 2
+    float4 for more), else the reduction kernel and its finalize.  Across
+    GPUs through peer memory the exchange runs inside the finalize CTA, or
+    as its own kernel after a one-CTA or one-cluster grid, so a reduction is
+    always two kernels; through NCCL the sums add the rank fold (NCCL's own
+    kernels are not counted)."""
+    if entry in MAP_ENTRIES:
         return 1
+    per_tile = 256 * 4 * (4 if len(TENSORS[entry]) == 1 else 2)
+    local = 1 if -(-n // per_tile) <= 8 else 2
+    if world == 1:
+        return local
     if peer:
-        per_tile = 256 * 4 * (4 if len(TENSORS[entry]) == 1 else 2)
-        return 1 if -(-n // per_tile) > 8 else 2
-    return 1 + (1 if entry != "max_value" else 0)
+        return 2
+    return local + (1 if entry != "max_value" else 0)
 
 
 def fmaf_f32(a: float, x, y):
@@ -1283,9 +1286,10 @@ def run_strong(args) -> None:
                            ("peer memory (NVLink P2P stores)" if comm.peer_exchange
                             else "NCCL all-gather / all-reduce")),
               "config": {"workload": "fixed global N sharded over the ranks: l2_norm_sq and "
-                                     "max_value at 2^30 (N(0,1), 1% x1e3 outliers); "
-                                     "affine_relu and pipeline_sum at 2^%s (U(-1,1))"
-                                     % ", 2^".join(str(k) for k in args.strong_sizes),
+                                     "max_value at 2^30 (N(0,1), 1 percent x1e3 outliers); "
+                                     "affine_relu and pipeline_sum at 2^"
+                                     + ", 2^".join(str(k) for k in args.strong_sizes)
+                                     + " (U(-1,1))",
                          "l2": "write-then-read 512 MiB flush before every timed call"},
               "checks_passed": bool(all_ok), "points": points})
     if comm is not None:

@@ -147,8 +147,8 @@ def render_header(package: str, plans: List[EntryPlan], multi_gpu: bool = True,
         if plan.program.entry_name in noalloc:
             lines.append(f"/* {plan.symbol}_noalloc: no counterpart in the reference.  The same "
                          "reduction for callers that cannot allocate device memory (no workspace "
-                         f"argument): its per-CTA values live in a static {NOALLOC_BYTES}-byte device "
-                         f"array ({NOALLOC_SLOTS} CTA slots) that the library holds on every GPU "
+                         f"argument): its per-CTA partials live in a static {NOALLOC_BYTES // 1024} KiB "
+                         f"device array ({NOALLOC_SLOTS} slots) that the library holds on every GPU "
                          f"that loads it; the grid is capped at {NOALLOC_SLOTS} CTAs, so any n >= 1 "
                          "fits.  The first call on a device, and the first after its context is "
                          "re-created (cudaDeviceReset), looks the array up: make it before any "
@@ -252,8 +252,10 @@ def render_entry(plan: EntryPlan, async_return: bool, multi_gpu: bool = True,
     if plan.kind == "map":
         L.append("  return loomb::launch_map(out, loom_in, n, loom_body, loom_stream);")
     else:
-        L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, "
-                 "loomb::workspace_scratch(workspace, n), out, nullptr, loom_stream);")
+        acc = "double" if plan.reduce_kind == "sum" else "float"
+        L.append(f"  {acc}* loom_partials = reinterpret_cast<{acc}*>(loomb::workspace_base(workspace));")
+        L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, loom_partials, "
+                 "loomb::partial_capacity(n), out, nullptr, loom_stream);")
     L.append("}")
     L.append("")
     # the reference entry: legacy default stream, synchronous unless built with
@@ -426,9 +428,7 @@ def render_comm_api(package: str) -> str:
 
 
 NOALLOC_SLOTS = 4096
-# a 256-byte header and the single-pass fold's view of the slot region (the
-# larger of its two views): 16 bytes per CTA and per group of 256 CTAs
-NOALLOC_BYTES = 256 + 16 * (NOALLOC_SLOTS + NOALLOC_SLOTS // 256)
+NOALLOC_BYTES = 8 * NOALLOC_SLOTS     # one fp64 partial per CTA
 
 
 def render_noalloc_scratch() -> str:
@@ -445,9 +445,9 @@ def render_noalloc_scratch() -> str:
         "// synchronise the whole device) is not allowed, or a C caller of the plain",
         "// ABI, whose reductions otherwise demand a sized workspace argument (only",
         "// maps have a _noworkspace form).  A _noalloc entry needs nothing but the",
-        "// inputs and the 1-float output: its per-CTA values go to the static array",
-        f"// below, a 256-byte header and {NOALLOC_SLOTS} CTA slots ({NOALLOC_BYTES} bytes in all),",
-        "// which every GPU that loads the library holds until the process exits.",
+        "// inputs and the 1-float output: its per-CTA partials go to the static",
+        f"// array below, {NOALLOC_SLOTS} fp64 slots ({NOALLOC_BYTES // 1024} KiB), which every GPU that loads",
+        "// the library holds until the process exits.",
         "//",
         "// Host code must not hand the array's name to a kernel: on the host it is",
         "// only a stand-in for the device symbol.  The entries look up the real",
@@ -458,10 +458,7 @@ def render_noalloc_scratch() -> str:
         "// by the context's unique id.  Make the first call on each device, and",
         "// the first after a reset, before any stream capture.",
         f"constexpr int kLoomNoallocSlots = {NOALLOC_SLOTS};",
-        "constexpr size_t kLoomNoallocBytes =",
-        "    loomb::kHeaderBytes + loomb::slot_region_bytes(kLoomNoallocSlots);",
-        f"static_assert(kLoomNoallocBytes == {NOALLOC_BYTES}, \"the documented size\");",
-        "static __device__ __align__(256) unsigned char loom_noalloc_scratch[kLoomNoallocBytes];",
+        "static __device__ __align__(256) double loom_noalloc_scratch[kLoomNoallocSlots];",
         "",
         "namespace {",
         "using LoomCtxGetCurrent = CUresult (*)(CUcontext*);",
@@ -543,17 +540,17 @@ def render_noalloc(plan: EntryPlan) -> str:
     sym = plan.symbol
     decls = _param_decls(plan) + ["int64_t n", "float* out", "void* stream"]
     L = [
-        f"// {sym}_noalloc -- {plan.program.entry_name} with its CTA values in the shared",
+        f"// {sym}_noalloc -- {plan.program.entry_name} with its CTA partials in the shared",
         "// static scratch above (no workspace argument).  The grid is capped at the",
         f"// {NOALLOC_SLOTS} slots (for large n each CTA then walks several tiles), so every",
         "// n >= 1 fits; while n needs no more tiles than that, it launches the same",
         "// grid as the workspace entry and gives the same bits, past that it differs",
-        "// only in rounding order.  Nothing in the array has to start at zero: the",
-        "// fold reads only slots that the same call wrote (each slot carries a",
-        "// check word tied to the call).  All calls of all _noalloc entries share",
-        "// the array, so two calls whose kernels overlap on the GPU (different",
-        "// streams, no ordering between them) race and corrupt each other's",
-        "// values: keep calls ordered on one stream.",
+        "// only in rounding order.  Nothing in the array has to start at zero:",
+        "// every slot the finalize kernel reads was written by the same call's",
+        "// first kernel.  All calls of all _noalloc entries share the array, so two",
+        "// calls whose kernels overlap on the GPU (different streams, no ordering",
+        "// between them) race and corrupt each other's partials: keep calls",
+        "// ordered on one stream.",
         f'extern "C" int {sym}_noalloc({", ".join(decls)}) {{',
     ]
     L += _validation(plan)
@@ -561,9 +558,11 @@ def render_noalloc(plan: EntryPlan) -> str:
     L.append("  const int loom_status = loom_noalloc_scratch_on(loomb::current_device(), &loom_scratch);")
     L.append("  if (loom_status != LOOM_STATUS_OK) return loom_status;")
     L += _body_setup(plan)
-    L.append("  const loomb::ReduceScratch loom_rs{static_cast<unsigned char*>(loom_scratch), "
-             "kLoomNoallocSlots};")
-    L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, loom_rs, out, nullptr, "
+    # the slot count is the array's, whatever the accumulator (fp64 for sums,
+    # fp32 for max), so the grid cap is kLoomNoallocSlots for both
+    acc = "double" if plan.reduce_kind == "sum" else "float"
+    L.append(f"  return loomb::launch_reduce<{_op(plan)}>(loom_in, n, loom_body, "
+             f"static_cast<{acc}*>(loom_scratch), (int64_t)kLoomNoallocSlots, out, nullptr, "
              "static_cast<cudaStream_t>(stream));")
     L += ["}", ""]
     return "\n".join(L)

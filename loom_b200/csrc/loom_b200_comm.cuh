@@ -372,13 +372,14 @@ template <class Op, class Body>
 inline int dist_local(const Ptrs<Body::kInputs>& in, int64_t n_local, const Body& body,
                       void* workspace, cudaStream_t stream) {
   RankSlots<Op> slots(workspace, n_local);
-  const ReduceScratch scratch = workspace_scratch(workspace, n_local > 0 ? n_local : 1);
+  auto* partials = reinterpret_cast<typename Op::Acc*>(workspace_base(workspace));
   if (n_local == 0) {
-    reduce_finalize_kernel<Op><<<1, kFinalizeThreads, 0, stream>>>(
-        scratch.slots<typename Op::Acc>(), 0, nullptr, slots.local);
+    reduce_finalize_kernel<Op><<<1, kFinalizeThreads, 0, stream>>>(partials, 0, nullptr,
+                                                                    slots.local);
     return launch_status();
   }
-  return launch_reduce<Op>(in, n_local, body, scratch, nullptr, slots.local, stream);
+  return launch_reduce<Op>(in, n_local, body, partials, partial_capacity(n_local), nullptr,
+                           slots.local, stream);
 }
 
 // Phase 2: the scalar collective (sum: all-gather of fp64; max: all-reduce).
@@ -444,6 +445,27 @@ __device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned l
 
 __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ unsigned long long acc_bits(double v) {
+  return (unsigned long long)__double_as_longlong(v);
+}
+__device__ __forceinline__ unsigned long long acc_bits(float v) { return __float_as_uint(v); }
+template <class Acc>
+__device__ __forceinline__ Acc bits_acc(unsigned long long b);
+template <>
+__device__ __forceinline__ double bits_acc<double>(unsigned long long b) {
+  return __longlong_as_double((long long)b);
+}
+template <>
+__device__ __forceinline__ float bits_acc<float>(unsigned long long b) {
+  return __uint_as_float((unsigned int)b);
 }
 
 // What an exchange needs, passed by value to the kernels that do one.
@@ -518,17 +540,6 @@ __device__ __forceinline__ void exchange_and_fold(const typename Op::Acc local,
   wait_stats[2] += 1;
 }
 
-// The multi-GPU finish of a single-pass reduction (thread 0 of the grid's
-// last CTA): this rank's total goes straight into the exchange, so the
-// reduction, its fold and the exchange are one kernel.
-template <class Op>
-struct PeerFinish {
-  PeerArgs a;
-  __device__ __forceinline__ void operator()(typename Op::Acc total) const {
-    exchange_and_fold<Op>(total, a);
-  }
-};
-
 // The exchange after a first stage that left this rank's value in `local`
 // (a one-CTA or one-cluster grid).
 template <class Op>
@@ -572,26 +583,20 @@ inline int launch_dependent_cta(Kern kernel, int threads, cudaStream_t stream, A
   return launch_status();
 }
 
-// This rank's shard reduced and exchanged through peer memory: one
-// single-pass kernel whose last CTA exchanges the total (launch_fold with
-// PeerFinish) where that applies; otherwise the first stage, then either the
-// fused finalize-and-exchange CTA (when the stage left partials) or the
-// exchange kernel alone.  An empty shard exchanges Op's identity.
+// This rank's shard reduced and exchanged through peer memory: the first
+// stage, then either the fused finalize-and-exchange CTA (when the stage
+// left partials) or the exchange kernel alone.  An empty shard exchanges
+// Op's identity.
 template <class Op, class Body>
 inline int dist_local_exchange(const Ptrs<Body::kInputs>& in, int64_t n_local, const Body& body,
                                void* workspace, float* out, const Comm* comm,
                                cudaStream_t stream) {
   RankSlots<Op> slots(workspace, n_local);
-  auto* partials =
-      workspace_scratch(workspace, n_local > 0 ? n_local : 1).slots<typename Op::Acc>();
+  auto* partials = reinterpret_cast<typename Op::Acc*>(workspace_base(workspace));
   const PeerArgs a = peer_args(comm, out);
   if (n_local == 0)
     return launch_dependent_cta(finalize_exchange_kernel<Op>, kFinalizeThreads, stream,
                                 static_cast<const typename Op::Acc*>(partials), 0, a);
-  int fold_status = LOOM_STATUS_OK;
-  if (launch_fold<Op>(in, n_local, body, workspace_scratch(workspace, n_local),
-                      PeerFinish<Op>{a}, stream, &fold_status))
-    return fold_status;
   unsigned pending = 0;
   const int st = launch_reduce_stage<Op>(in, n_local, body, partials, partial_capacity(n_local),
                                          nullptr, slots.local, stream, &pending);

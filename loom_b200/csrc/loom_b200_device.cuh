@@ -53,16 +53,6 @@ constexpr int64_t kMinTileElems = (int64_t)kThreads * 4;  // smallest tile of an
 constexpr int64_t kMaxGrid = (int64_t)1 << 30;
 constexpr int kMaxDevices = 64;
 constexpr int kMaxClusterCtas = 8;       // portable thread-block cluster size
-constexpr int kFoldGroup = kThreads;     // CTAs per first-level group of the single-pass fold
-static_assert(kMaxPartials / kFoldGroup <= kThreads, "one group total per folding thread");
-constexpr unsigned long long kFoldTimeoutNs = 10000000000ull;  // bound of a fold's wait
-
-// How the CTAs of a reduce_vec_kernel grid hand on their values (a
-// single-pass grid, reduce_fold_kernel, folds them with fold_in_last_cta).
-enum ReduceMode {
-  kToPartials = 0,  // one Acc per CTA into `partials` (a finalize kernel folds them)
-  kClusterFold = 1, // the grid is one cluster: rank 0 folds through DSMEM
-};
 
 // float4 loads per input per thread per tile (measured best on B200).
 template <int K>
@@ -72,14 +62,6 @@ struct MapUnroll {
 template <int K>
 struct ReduceUnroll {
   static constexpr int value = K == 1 ? 4 : 2;
-};
-// Resident CTAs per SM a single-pass reduction is compiled for (its
-// register budget: 32 per thread for one input, 40 for more, what the
-// streaming loop needs), so that the fold's code does not lower the
-// streaming loop's occupancy.
-template <int K>
-struct FoldMinCtas {
-  static constexpr int value = K == 1 ? 8 : 6;
 };
 
 template <int K>
@@ -107,84 +89,6 @@ __device__ __forceinline__ void allow_dependent_launch() {
 
 __device__ __forceinline__ void wait_for_prerequisite_grid() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-// ---------------------------------------------------------------------------
-// clocks, bit views, and the single-pass fold's slots
-
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ unsigned long long acc_bits(double v) {
-  return (unsigned long long)__double_as_longlong(v);
-}
-__device__ __forceinline__ unsigned long long acc_bits(float v) { return __float_as_uint(v); }
-template <class Acc>
-__device__ __forceinline__ Acc bits_acc(unsigned long long b);
-template <>
-__device__ __forceinline__ double bits_acc<double>(unsigned long long b) {
-  return __longlong_as_double((long long)b);
-}
-template <>
-__device__ __forceinline__ float bits_acc<float>(unsigned long long b) {
-  return __uint_as_float((unsigned int)b);
-}
-
-// One CTA's value in the single-pass fold, with a check word that ties the
-// value to the call that wrote it.  The slots live in the caller's workspace
-// (or the no-allocation scratch), whose contents are arbitrary before the
-// first call and hold older calls' slots afterwards, and nothing zeroes them:
-// a slot counts only when check == fold_check(epoch + 1, bits), with epoch
-// the workspace's call count read by this call.  A slot left by an older
-// call fails the check (its epoch differs), and so does a slot whose two
-// words were seen half-written, unless the stale bits equal the new ones,
-// which then gives the same value anyway.  Foreign data passes only by a
-// 64-bit coincidence.  So the writers need no fence and the readers no
-// counter that has to start at zero.
-struct FoldSlot {
-  unsigned long long bits;
-  unsigned long long check;
-};
-
-// The 64-bit finalizer of splitmix64 (G. Steele, D. Lea, C. Flood, "Fast
-// splittable pseudorandom number generators", OOPSLA 2014): a bijective mix
-// in which every input bit affects every output bit.
-__device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
-  z ^= z >> 30;
-  z *= 0xbf58476d1ce4e5b9ull;
-  z ^= z >> 27;
-  z *= 0x94d049bb133111ebull;
-  z ^= z >> 31;
-  return z;
-}
-
-__device__ __forceinline__ unsigned long long fold_check(unsigned long long epoch,
-                                                         unsigned long long bits) {
-  return mix64(bits ^ mix64(epoch ^ 0x9e3779b97f4a7c15ull));
-}
-
-__device__ __forceinline__ void store_slot(FoldSlot* p, unsigned long long bits,
-                                           unsigned long long check) {
-  asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(bits), "l"(check)
-               : "memory");
-}
-
-__device__ __forceinline__ FoldSlot load_slot(const FoldSlot* p) {
-  FoldSlot v;
-  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];"
-               : "=l"(v.bits), "=l"(v.check)
-               : "l"(p)
-               : "memory");
-  return v;
-}
-
-__device__ __forceinline__ unsigned long long load_epoch(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
 }
 
 template <class Body>
@@ -374,149 +278,20 @@ __device__ __forceinline__ typename Op::Chunk fold_chunks(const typename Op::Chu
 }
 
 
-// Waits until `slot` passes its check for epoch `next` and returns its
-// bits.  The wait is bounded by kFoldTimeoutNs of %globaltimer (from t0) and
-// by a poll count; when it runs out, `expired` is set and 0 returned.
-__device__ __forceinline__ unsigned long long wait_slot(const FoldSlot* slot,
-                                                        unsigned long long next,
-                                                        unsigned long long t0, bool& expired) {
-  constexpr unsigned long long kMaxPolls = 1ull << 27;
-  for (unsigned long long polls = 0; !expired; ++polls) {
-    const FoldSlot v = load_slot(slot);
-    if (v.check == fold_check(next, v.bits)) return v.bits;
-    if (polls > kMaxPolls || global_ns() - t0 > kFoldTimeoutNs) expired = true;
-    else __nanosleep(64);
-  }
-  return 0;
-}
-
-// One level of the fold, in all threads of a folding CTA: thread t takes
-// value t of the `count` (<= kThreads) values first[0..count): its own
-// value `mine` (from shared memory) at position `own`, or the bits of a slot
-// once it passes its check; then the block reduce (result in thread 0).
-// Every thread reaches the block reduce, also after a wait that ran out.
-template <class Op>
-__device__ __forceinline__ typename Op::Acc fold_level(const FoldSlot* first, int count, int own,
-                                                       typename Op::Acc mine,
-                                                       unsigned long long next,
-                                                       unsigned long long t0, int* expired_s) {
-  using Acc = typename Op::Acc;
-  Acc a = Op::init();
-  const int t = (int)threadIdx.x;
-  if (t == own) {
-    a = mine;
-  } else if (t < count) {
-    bool expired = false;
-    const unsigned long long bits = wait_slot(first + t, next, t0, expired);
-    if (expired) *expired_s = 1;
-    else a = bits_acc<Acc>(bits);
-  }
-  return block_reduce<Op>(a);
-}
-
-// The single-pass fold, in every CTA of a reduce_fold_kernel grid after its
-// block reduce (`acc` and `epoch` valid in thread 0).  The CTAs form groups
-// of kFoldGroup consecutive CTAs.  Every CTA but the last of its group
-// stores its value in its FoldSlot and exits.  The last CTA of a group (the
-// last of it the hardware dispatches, so it rarely waits long) polls its
-// group's slots until each passes its check, folds the group's values in a
-// fixed order (value t in thread t, then the block reduce) and stores the
-// group's total in the group's slot, which follows the grid's CTA slots.
-// The grid's last CTA does the same for its own group and then folds the
-// group totals the same way.  The result depends only on the grid, and at
-// most one CTA per group ever waits, far fewer CTAs than the SMs hold, so a
-// waiting CTA never keeps the CTAs it waits for from running.  A wait that
-// runs out (kFoldTimeoutNs) makes the group's total, and so the result, NaN.
-// The last CTA finally advances the workspace's epoch, which the next call
-// on this workspace (ordered after this one on the stream) reads, and hands
-// the total to `finish` (its thread 0): StoreTotal on one GPU, the scalar
-// exchange with the other GPUs' totals across GPUs.
-template <class Op, class Finish>
-__device__ __forceinline__ void fold_in_last_cta(typename Op::Acc acc, unsigned long long epoch,
-                                                 FoldSlot* __restrict__ slots,
-                                                 unsigned long long* __restrict__ header,
-                                                 const Finish& finish) {
-  using Acc = typename Op::Acc;
-  const int grid = (int)gridDim.x;
-  const int me = (int)blockIdx.x;
-  const int group = me / kFoldGroup;
-  const int groups = (grid + kFoldGroup - 1) / kFoldGroup;
-  const int group_first = group * kFoldGroup;
-  const int group_last = min(grid, group_first + kFoldGroup) - 1;
-  FoldSlot* group_slots = slots + grid;
-  if (me != group_last) {
-    if (threadIdx.x == 0) {
-      const unsigned long long bits = acc_bits(acc);
-      store_slot(slots + me, bits, fold_check(epoch + 1, bits));
-    }
-    return;
-  }
-  __shared__ unsigned long long next_s;
-  __shared__ Acc value_s;
-  __shared__ int expired_s;
-  if (threadIdx.x == 0) {
-    next_s = epoch + 1;
-    value_s = acc;
-    expired_s = 0;
-  }
-  __syncthreads();   // also ends the reads of the block reduce's scratch above
-  const unsigned long long next = next_s;
-  const unsigned long long t0 = global_ns();
-  Acc total = fold_level<Op>(slots + group_first, group_last - group_first + 1,
-                             me - group_first, value_s, next, t0, &expired_s);
-  __syncthreads();   // expired_s and the block reduce's scratch
-  if (threadIdx.x == 0 && expired_s)
-    total = bits_acc<Acc>(sizeof(Acc) == 8 ? 0x7ff8000000000000ull : 0x7fc00000ull);  // NaN
-  if (me != grid - 1) {
-    if (threadIdx.x == 0) {
-      const unsigned long long bits = acc_bits(total);
-      store_slot(group_slots + group, bits, fold_check(next, bits));
-    }
-    return;
-  }
-  if (groups > 1) {
-    if (threadIdx.x == 0) value_s = total;
-    __syncthreads();
-    total = fold_level<Op>(group_slots, groups, group, value_s, next, t0, &expired_s);
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    header[0] = next;
-    finish(expired_s ? bits_acc<Acc>(sizeof(Acc) == 8 ? 0x7ff8000000000000ull : 0x7fc00000ull)
-                     : total);
-  }
-}
-
-// The single-GPU finish of a single-pass reduction (thread 0 of the grid's
-// last CTA): the fp32 result to out[0] and/or the full-precision value to
-// partial_out[0] (a NaN when the fold's wait ran out).
-template <class Op>
-struct StoreTotal {
-  float* out;
-  typename Op::Acc* partial_out;
-  __device__ __forceinline__ void operator()(typename Op::Acc total) const {
-    if (out != nullptr) out[0] = Op::to_float(total);
-    if (partial_out != nullptr) partial_out[0] = total;
-  }
-};
-
-// How the CTAs of a reduce_vec_kernel grid finish (`acc` valid in thread 0):
-//  * kToPartials: a one-CTA grid is already complete and writes the result
-//    itself; otherwise each CTA writes its partial for a finalize kernel;
-//  * kClusterFold: the whole grid (at most kMaxClusterCtas CTAs) is one
-//    thread-block cluster; each CTA leaves its value in its shared memory,
-//    and CTA rank 0 folds them in rank order through distributed shared
-//    memory, so a small reduction is complete in one launch.  The second
-//    cluster barrier keeps every CTA's shared memory alive until rank 0 has
-//    read it.
-// (Single-pass grids fold through fold_in_last_cta instead.)
-template <class Op, int kMode>
+// A one-CTA reduction is already complete in that CTA: it writes the result
+// itself and the launcher skips the finalize kernel.  With kCluster the whole
+// grid (at most kMaxClusterCtas CTAs) is one thread-block cluster: each CTA
+// leaves its value in its shared memory, and CTA rank 0 folds them in rank
+// order through distributed shared memory, so a small reduction is complete
+// in one launch.  The second cluster barrier keeps every CTA's shared memory
+// alive until rank 0 has read it.  `acc` is valid in thread 0 only.
+template <class Op, bool kCluster>
 __device__ __forceinline__ void store_reduction(typename Op::Acc acc,
                                                 typename Op::Acc* __restrict__ partials,
                                                 float* __restrict__ out,
                                                 typename Op::Acc* __restrict__ partial_out) {
   using Acc = typename Op::Acc;
-  if constexpr (kMode == kClusterFold) {
+  if constexpr (kCluster) {
     namespace cg = cooperative_groups;
     __shared__ Acc cta_value;
     cg::cluster_group cluster = cg::this_cluster();
@@ -532,30 +307,21 @@ __device__ __forceinline__ void store_reduction(typename Op::Acc acc,
     }
     cluster.sync();
     return;
+  }
+  if (threadIdx.x != 0) return;
+  if (gridDim.x == 1) {
+    if (out != nullptr) out[0] = Op::to_float(acc);
+    if (partial_out != nullptr) partial_out[0] = acc;
   } else {
-    if (threadIdx.x != 0) return;
-    if (gridDim.x == 1) {
-      if (out != nullptr) out[0] = Op::to_float(acc);
-      if (partial_out != nullptr) partial_out[0] = acc;
-    } else {
-      partials[blockIdx.x] = acc;
-    }
+    partials[blockIdx.x] = acc;
   }
 }
 
-// The vector reduction of one CTA's tiles, then the CTA's block reduce
-// (result in thread 0).  With `header` (single-pass grids), thread 0 also
-// reads the workspace's fold epoch into `epoch`: here, not at the start, so
-// that it holds no register through the streaming loop, and its latency
-// hides behind the block reduce.  The grid's last CTA advances the epoch
-// only after every other CTA's slot is in, and each CTA writes its slot
-// after this read, so every CTA of a call reads the same value.
-template <class Op, class Body, int U>
-__device__ __forceinline__ typename Op::Acc reduce_tiles(const Ptrs<Body::kInputs>& in,
-                                                         const int64_t n, const int64_t head,
-                                                         const Body& body,
-                                                         const unsigned long long* header,
-                                                         unsigned long long& epoch) {
+template <class Op, class Body, int U, bool kCluster = false>
+__global__ void __launch_bounds__(kThreads)
+reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInputs> in,
+                  const int64_t n, const int64_t head, const Body body, float* __restrict__ out,
+                  typename Op::Acc* __restrict__ partial_out) {
   allow_dependent_launch();
   wait_for_prerequisite_grid();
   constexpr int K = Body::kInputs;
@@ -607,34 +373,8 @@ __device__ __forceinline__ typename Op::Acc reduce_tiles(const Ptrs<Body::kInput
     else if (r >= 4 && (int64_t)(r - 4) < n - tail0) i = tail0 + (r - 4);
     if (i >= 0) acc = Op::absorb(acc, apply1(body, in, i));
   }
-  if (header != nullptr && threadIdx.x == 0) epoch = load_epoch(header);
-  return block_reduce<Op>(acc);
-}
-
-// The stage of a two-launch reduction (kToPartials: `partials` holds one Acc
-// per CTA) or a one-cluster grid (kClusterFold).
-template <class Op, class Body, int U, int kMode = kToPartials>
-__global__ void __launch_bounds__(kThreads)
-reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInputs> in,
-                  const int64_t n, const int64_t head, const Body body, float* __restrict__ out,
-                  typename Op::Acc* __restrict__ partial_out) {
-  unsigned long long epoch = 0;
-  const typename Op::Acc acc = reduce_tiles<Op, Body, U>(in, n, head, body, nullptr, epoch);
-  store_reduction<Op, kMode>(acc, partials, out, partial_out);
-}
-
-// The single-pass reduction: `slots` is the workspace's FoldSlot region and
-// `header` its header; `finish` takes the total (StoreTotal on one GPU).
-// Compiled for the streaming loop's occupancy (FoldMinCtas) so that the
-// fold's code costs it none.
-template <class Op, class Body, int U, class Finish>
-__global__ void __launch_bounds__(kThreads, FoldMinCtas<Body::kInputs>::value)
-reduce_fold_kernel(FoldSlot* __restrict__ slots, const Ptrs<Body::kInputs> in, const int64_t n,
-                   const int64_t head, const Body body, unsigned long long* __restrict__ header,
-                   const Finish finish) {
-  unsigned long long epoch = 0;
-  const typename Op::Acc acc = reduce_tiles<Op, Body, U>(in, n, head, body, header, epoch);
-  fold_in_last_cta<Op>(acc, epoch, slots, header, finish);
+  acc = block_reduce<Op>(acc);
+  store_reduction<Op, kCluster>(acc, partials, out, partial_out);
 }
 
 template <class Op, class Body>
@@ -677,7 +417,7 @@ reduce_scalar_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::k
     }
   }
   acc = block_reduce<Op>(acc);
-  store_reduction<Op, kToPartials>(acc, partials, out, partial_out);
+  store_reduction<Op, false>(acc, partials, out, partial_out);
 }
 
 // One CTA of kFinalizeThreads folds `count` CTA partials in a fixed order:

@@ -6,10 +6,8 @@
 // :2344-2422): instead of fixed block-count caps (4096 / 32768 blocks of 256
 // threads) and a host loop of combine launches, every kernel gets one CTA per
 // tile (a reduction at most kMaxPartials CTAs, or fewer when the caller's
-// scratch has fewer slots), and a reduction is one launch: a thread-block
-// cluster up to 8 CTAs, a grid that folds its CTAs' values itself above
-// (two launches, the stage and a finalize CTA, only for pointers that
-// disagree mod 16).
+// scratch has fewer partial slots), and a reduction is one launch when its
+// grid fits one thread-block cluster (at most 8 CTAs) and two otherwise.
 //
 // Nothing here allocates device memory and nothing holds device state.
 #pragma once
@@ -33,17 +31,14 @@ namespace loomb {
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Bytes of workspace region reserved after the CTA slots for the multi-GPU
-// path: one local fp64 value at +0 and the rank gather at +64.
+// Bytes of workspace region reserved after the CTA partials for the
+// multi-GPU path: one local fp64 value at +0 and the rank gather at +64.
 constexpr size_t kRankScratchBytes = 256;
 constexpr int kMaxRanks = 24;
-// The workspace header: +0 u64, the number of single-pass folds made on
-// this workspace (the fold's epoch; arbitrary before the first).
-constexpr size_t kHeaderBytes = 256;
 
-// Number of CTA slots a reduction over n elements may use: one per smallest
-// tile, at most kMaxPartials.  The workspace size and every workspace-backed
-// reduction launch use this same bound.
+// Number of CTA partial slots a reduction over n elements may use: one per
+// smallest tile, at most kMaxPartials.  The workspace size and every
+// workspace-backed reduction launch use this same bound.
 inline int64_t partial_capacity(int64_t n) {
   int64_t c = ceil_div(n, kMinTileElems);
   if (c < 1) c = 1;
@@ -51,25 +46,12 @@ inline int64_t partial_capacity(int64_t n) {
   return c;
 }
 
-// Bytes of the per-CTA slot region for `cap` CTAs: it holds either an fp64
-// (or fp32) partial per CTA, for the two-launch path, or the single-pass
-// fold's 16-byte FoldSlots, one per CTA and then one per group of
-// kFoldGroup CTAs; one call uses one of the two views.
-constexpr size_t slot_region_bytes(int64_t cap) {
-  const size_t partial_bytes = (size_t)cap * sizeof(double);
-  const size_t fold_bytes =
-      (size_t)(cap + (cap + kFoldGroup - 1) / kFoldGroup) * sizeof(FoldSlot);
-  const size_t bytes = partial_bytes > fold_bytes ? partial_bytes : fold_bytes;
-  return (bytes + 255) / 256 * 256;
-}
-
 // Workspace layout, carved from the first 256-byte boundary at or after the
 // caller's pointer (the trailing 256 bytes of slack make any base address
-// fit): [0, 256) header, [256, 256 + slot_region_bytes) CTA slots, then
-// kRankScratchBytes of rank scratch.  Nothing in it has to start at any
-// particular value.
+// fit): [0, P) CTA partials (fp64 slots), [P, P + kRankScratchBytes) rank
+// scratch.
 inline size_t rank_scratch_offset(int64_t n) {
-  return kHeaderBytes + slot_region_bytes(partial_capacity(n));
+  return align_up((size_t)partial_capacity(n) * sizeof(double), 256);
 }
 
 inline size_t reduce_workspace_bytes(int64_t n) {
@@ -80,23 +62,6 @@ inline size_t reduce_workspace_bytes(int64_t n) {
 // First 256-byte boundary at or after `workspace`.
 inline unsigned char* workspace_base(void* workspace) {
   return reinterpret_cast<unsigned char*>(align_up((size_t)(uintptr_t)workspace, 256));
-}
-
-// A reduction's scratch: the header and the CTA slot region of a caller's
-// workspace or of a library-owned array, 256-byte aligned, with room for
-// `cap` CTAs.
-struct ReduceScratch {
-  unsigned char* base;
-  int64_t cap;
-  unsigned long long* header() const { return reinterpret_cast<unsigned long long*>(base); }
-  template <class T>
-  T* slots() const {
-    return reinterpret_cast<T*>(base + kHeaderBytes);
-  }
-};
-
-inline ReduceScratch workspace_scratch(void* workspace, int64_t n) {
-  return ReduceScratch{workspace_base(workspace), partial_capacity(n)};
 }
 
 inline int current_device() {
@@ -183,8 +148,8 @@ inline bool launch_cluster_reduce(unsigned grid, const Ptrs<Body::kInputs>& in, 
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   typename Op::Acc* no_partials = nullptr;
-  if (cudaLaunchKernelEx(&cfg, reduce_vec_kernel<Op, Body, U, kClusterFold>, no_partials, in, n,
-                         head, body, out, partial_out) == cudaSuccess)
+  if (cudaLaunchKernelEx(&cfg, reduce_vec_kernel<Op, Body, U, true>, no_partials, in, n, head,
+                         body, out, partial_out) == cudaSuccess)
     return true;
   cudaGetLastError();
   return false;
@@ -277,53 +242,16 @@ inline int launch_reduce_stage(const Ptrs<Body::kInputs>& in, int64_t n, const B
   return st;
 }
 
-// The single-pass reduction of body(in[...][i]) over [0, n) with Op, where
-// it applies (every pointer congruent mod 16 and a grid of more than
-// kMaxClusterCtas CTAs): one launch whose CTAs fold their values inside the
-// grid with the FoldSlots and header of `scratch`, the total going to
-// `finish` (StoreTotal, or the multi-GPU exchange).  Returns false, having
-// launched nothing, where it does not apply; *status is the launch's status.
-template <class Op, class Body, class Finish>
-inline bool launch_fold(const Ptrs<Body::kInputs>& in, int64_t n, const Body& body,
-                        const ReduceScratch& scratch, const Finish& finish, cudaStream_t stream,
-                        int* status) {
-  if (n <= 0 || scratch.cap < 1 || !pointers_aligned4(in, nullptr) || !congruent16(in, in.p[0]))
-    return false;
-  constexpr int U = ReduceUnroll<Body::kInputs>::value;
-  const int64_t head = head_elems(in.p[0], n);
-  const int64_t nvec = (n - head) >> 2;
-  const unsigned grid = clamp_grid(ceil_div(nvec, (int64_t)kThreads * U), scratch.cap);
-  if (grid <= (unsigned)kMaxClusterCtas) return false;
-  launch_pdl(reduce_fold_kernel<Op, Body, U, Finish>, grid, stream, scratch.slots<FoldSlot>(), in,
-             n, head, body, scratch.header(), finish);
-  *status = launch_status();
-  return true;
-}
-
 // Reduces body(in[...][i]) over [0, n) with Op into out[0] (fp32) and/or
-// partial_out[0] (Op::Acc), with the CTA slots and header of `scratch`:
-//  * one CTA, or a grid of up to kMaxClusterCtas launched as one cluster:
-//    one launch, no slots used;
-//  * more CTAs (congruent pointers): one launch that folds every CTA's
-//    FoldSlot inside the grid (launch_fold);
-//  * pointers that disagree mod 16 (and a refused cluster launch): the
-//    first stage, then the finalize CTA over the partials.
-// Every path folds in an order fixed by the grid alone, so the result is
-// bit-reproducible.
+// partial_out[0] (Op::Acc): the first stage, then the finalize CTA where
+// partials are left.
 template <class Op, class Body>
 inline int launch_reduce(const Ptrs<Body::kInputs>& in, int64_t n, const Body& body,
-                         const ReduceScratch& scratch, float* out,
+                         typename Op::Acc* partials, int64_t max_partials, float* out,
                          typename Op::Acc* partial_out, cudaStream_t stream) {
-  using Acc = typename Op::Acc;
-  if (n <= 0 || scratch.cap < 1) return LOOM_STATUS_INVALID_ARGUMENT;
-  if (!pointers_aligned4(in, nullptr)) return LOOM_STATUS_INVALID_ARGUMENT;
-  int st = LOOM_STATUS_OK;
-  if (launch_fold<Op>(in, n, body, scratch, StoreTotal<Op>{out, partial_out}, stream, &st))
-    return st;
-  Acc* partials = scratch.slots<Acc>();
   unsigned pending = 0;
-  st = launch_reduce_stage<Op>(in, n, body, partials, scratch.cap, out, partial_out, stream,
-                               &pending);
+  const int st = launch_reduce_stage<Op>(in, n, body, partials, max_partials, out, partial_out,
+                                         stream, &pending);
   if (st != LOOM_STATUS_OK || pending == 0) return st;
   return launch_finalize<Op>(partials, (int)pending, out, partial_out, stream);
 }

@@ -58,16 +58,12 @@ def test_warmup_below_three_is_refused():
 
 def test_launch_counts():
     n = 1 << 28
-    # one GPU: every entry is one kernel (a reduction folds inside its grid)
-    for size in (4096, 1 << 22, n):
-        assert all(bench.launches_per_call(e, 1, size) == 1 for e in bench.ENTRIES)
+    assert [bench.launches_per_call(e, 1, n) for e in bench.ENTRIES] == [1, 1, 2, 2, 2, 1, 2]
     assert [bench.launches_per_call(e, 4, n, peer=False) for e in bench.ENTRIES] == \
-        [1, 1, 2, 2, 1, 1, 2]
-    # across GPUs through peer memory the exchange runs inside the reduction
-    # kernel, except after a one-CTA or one-cluster grid
-    assert all(bench.launches_per_call(e, 4, n, peer=True) == 1 for e in bench.ENTRIES)
-    assert [bench.launches_per_call(e, 4, 4096, peer=True) for e in bench.ENTRIES] == \
+        [1, 1, 3, 3, 2, 1, 3]
+    assert [bench.launches_per_call(e, 4, n, peer=True) for e in bench.ENTRIES] == \
         [1, 1, 2, 2, 2, 1, 2]
+    assert all(bench.launches_per_call(e, 1, 4096) == 1 for e in bench.ENTRIES)
 
 
 def test_fmaf_f32_is_correctly_rounded():

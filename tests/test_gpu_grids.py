@@ -1,22 +1,16 @@
-"""The single-pass reduction: a grid of more than 8 CTAs that folds its
-CTAs' values itself (fold_in_last_cta in loom_b200_device.cuh): groups of
-256 consecutive CTAs, whose last CTA folds the group, and the grid's last
-CTA, which folds the group totals.
+"""Reductions over grids of every shape, and the caller's workspace.
 
-The CTAs leave their values in slots of the caller's workspace, each with a
-check word tied to the workspace's epoch (the number of folds made on it),
-and nothing zeroes the workspace.  These tests check, against the CPU
-oracle (max bit-exact, sums within 1e-6 * max(1, log2 n) * |ref|):
+A reduction of more than 8 CTAs writes one partial per CTA into the caller's
+workspace and a finalize CTA folds them.  Against the CPU oracle (max
+bit-exact, sums within 1e-6 * max(1, log2 n) * |ref|):
 
-* grid sizes around the fold's boundaries: 9 CTAs (the smallest fold),
-  256 and 257 (one group, then two), 4097, and 32768 and more tiles (the
-  grid's cap, where CTAs take several tiles), aligned and with a 3-element
-  head;
-* a workspace reused by calls of different sizes, whose older slots must
-  not pass for the current call's;
+* grid sizes 9 (the smallest two-launch grid), 255-257, 4097, and 32768 and
+  more tiles (the partial-slot cap, where CTAs take several tiles), aligned
+  and with a 3-element head;
 * workspaces filled beforehand with zeros, ones, 0xff bytes and random
-  bytes;
-* the epoch, which every fold advances by one, and an epoch wound back;
+  bytes: nothing in a workspace has to start at any value;
+* one workspace reused by calls of different sizes and entries: a call
+  reads only the partials it wrote;
 * determinism: the same inputs give the same bits.
 """
 
@@ -62,7 +56,7 @@ def call_with_workspace(pkg, entry, dev, ws):
 
 
 @pytest.mark.parametrize("entry", ["dot", "l2_norm_sq", "max_value", "pipeline_sum"])
-def test_sizes_around_the_fold_boundaries(suite_pkg, oracle, entry):
+def test_grid_sizes(suite_pkg, oracle, entry):
     tile = tile_of(entry)
     sizes = [(9, 0), (9, 5), (255, 1), (256, 0), (256, 1), (257, 0), (4097, 3)]
     if entry in ("dot", "l2_norm_sq"):
@@ -96,7 +90,7 @@ def _workspace(pkg, entry, n, fill):
 
 @pytest.mark.parametrize("fill", ["zeros", "ones", "ff", "random"])
 def test_any_prior_workspace_contents(suite_pkg, oracle, fill):
-    n = 1000 * 2048 + 7            # 1001 tiles of a two-input reduction: four groups
+    n = 1000 * 2048 + 7            # 1001 tiles of a two-input reduction
     inp = workloads.entry_inputs("dot", n, seed_offset=77)
     ref = oracle.run("dot", inp)
     dev = {k: to_device(v) for k, v in inp.items()}
@@ -105,9 +99,9 @@ def test_any_prior_workspace_contents(suite_pkg, oracle, fill):
         check("dot", call_with_workspace(suite_pkg, "dot", dev, ws), ref, inp, n)
 
 
-def test_reused_workspace_with_stale_slots(suite_pkg, oracle):
+def test_reused_workspace(suite_pkg, oracle):
     # one workspace, calls that alternate between grids and entries: each call
-    # must read only the slots it wrote, never a slot left by an earlier call
+    # must read only the partials it wrote, never one left by an earlier call
     big = 4096 * 2048 - 5
     ws = _workspace(suite_pkg, "dot", big, "random")
     cases = []
@@ -123,25 +117,7 @@ def test_reused_workspace_with_stale_slots(suite_pkg, oracle):
             check(entry, call_with_workspace(suite_pkg, entry, dev, ws), ref, inp, n)
 
 
-def test_epoch_advances_once_per_fold(suite_pkg):
-    n = 600 * 2048
-    inp = workloads.entry_inputs("dot", n, seed_offset=3)
-    dev = {k: to_device(v) for k, v in inp.items()}
-    ws = _workspace(suite_pkg, "dot", n, "zeros")
-    base = (-ws.data_ptr()) % 256            # the header starts at the first 256-byte boundary
-    header = ws[base:base + 8]
-    first = call_with_workspace(suite_pkg, "dot", dev, ws)
-    e1 = int(header.view(torch.int64).item())
-    for _ in range(4):
-        assert call_with_workspace(suite_pkg, "dot", dev, ws) == first
-    assert int(header.view(torch.int64).item()) == e1 + 4
-    # wound back: the next call checks for epoch e1, whose slots later calls
-    # overwrote with other check words, so it must wait for its own values
-    header.view(torch.int64).fill_(e1 - 1)
-    assert call_with_workspace(suite_pkg, "dot", dev, ws) == first
-
-
-def test_fold_is_deterministic(suite_pkg):
+def test_reductions_are_deterministic_over_grids(suite_pkg):
     for entry, n in (("dot", 2047 * 2048 + 3), ("l2_norm_sq", 1500 * 4096 + 1),
                      ("pipeline_sum", 3000 * 2048)):
         inp = workloads.entry_inputs(entry, n, seed_offset=11)

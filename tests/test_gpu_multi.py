@@ -74,6 +74,10 @@ def test_multi_one_process(suite_pkg, oracle, n, exchange):
                 assert host == results[0]
         for c in comms:
             c.check()
+            stats = c.exchange_stats(reset=True)
+            # every reduction exchanged once per device on the peer path
+            assert stats["exchanges"] == (4 if exchange == "peer" else 0), stats
+            assert stats["max_us"] >= stats["total_us"] / max(1, stats["exchanges"])
     finally:
         for c in comms:
             c.destroy()
@@ -148,15 +152,18 @@ def test_dist_one_process_per_gpu(oracle):
         _check(entry, got[entry], oracle.run(entry, full), full, n)
 
 
-def test_exchange_wait_is_bounded(suite_pkg):
+@pytest.mark.parametrize("n", [4096, 1 << 20])
+def test_exchange_wait_is_bounded(suite_pkg, n):
     # Only device 0 takes part: its exchange waits for a value that nobody
     # sends, gives up after its time limit (1 s here), records the failure
-    # and returns NaN.  The device stays usable.
+    # and returns NaN.  The device stays usable.  n = 4096 is a one-cluster
+    # grid followed by the exchange kernel; n = 2^20 is a grid of 512 CTAs
+    # followed by the finalize CTA that runs the exchange.
     comms = suite_pkg.comm_init_all([0, 1])
     try:
         assert comms[0].peer_exchange
         comms[0].set_timeout_ms(1000)
-        x = torch.ones(4096, device="cuda:0")
+        x = torch.ones(n, device="cuda:0")
         with torch.cuda.device(0):
             out = suite_pkg["dot"].dist(comms[0], x=x, y=x)
             torch.cuda.synchronize()
@@ -164,7 +171,7 @@ def test_exchange_wait_is_bounded(suite_pkg):
         with pytest.raises(Exception) as info:
             comms[0].check()
         assert info.value.status == 4          # LOOM_STATUS_COMM_ERROR
-        assert float(suite_pkg["dot"](x=x, y=x).cpu()[0]) == 4096.0
+        assert float(suite_pkg["dot"](x=x, y=x).cpu()[0]) == float(n)
     finally:
         for c in comms:
             c.destroy()

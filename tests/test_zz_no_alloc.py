@@ -2,8 +2,8 @@
 the library device memory -- a framework that owns the GPU's memory through
 its own allocator, a loop where cudaMalloc's possible device-wide
 synchronisation is not allowed, a plain C caller with no workspace to pass.
-The entry takes no workspace argument; its per-CTA values live in a static
-device array inside the library (4096 CTA slots and a small header).
+The entry takes no workspace argument; its per-CTA partials live in a static
+device array inside the library (4096 fp64 slots, 32 KiB).
 
 Two calls in a row through the C ABI, each checked against the CPU oracle's
 fp64 sum of the same fp32 products with the sum bar of the other tests,
@@ -12,7 +12,7 @@ fp64 sum of the same fp32 products with the sum bar of the other tests,
 * n = 2^24 + 3 needs 8192 tiles, so the entry caps its grid at the array's
   4096 slots (each CTA walks two tiles) and fills every slot;
 * n = 2^20 + 5 then runs a grid of 513 CTAs over the first call's leftovers:
-  its fold must use only the 513 values this call wrote.  With the same
+  its finalize must read only the 513 partials this call wrote.  With the same
   grid as the workspace entry loom_kernels_dot, it must also give the same
   bits as that entry.
 
