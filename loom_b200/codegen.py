@@ -168,6 +168,11 @@ def render_header(package: str, plans: List[EntryPlan], multi_gpu: bool = True,
     return "\n".join(lines)
 
 
+# Reduction families whose values are never negative (an fp32 value times
+# itself): the square families of the reference's reduction classification.
+NONNEGATIVE_FAMILIES = ("norm-square", "delta-square")
+
+
 def render_body_struct(plan: EntryPlan) -> str:
     k = len(plan.slots)
     name = f"LoomBody_{plan.symbol}"
@@ -175,7 +180,12 @@ def render_body_struct(plan: EntryPlan) -> str:
            + (f" ({plan.reduce_kind})" if plan.reduce_kind else "")
            + f", slots [{', '.join(plan.slots)}], family {plan.family}",
            f"struct {name} {{",
-           f"  static constexpr int kInputs = {k};"]
+           f"  static constexpr int kInputs = {k};",
+           # a reduction over squares (x*x, (a-b)*(a-b)) never adds a negative
+           # value, so its sums may add within a tile in fp32 (Chunking)
+           "  static constexpr bool kNonNegative = "
+           + ("true;" if plan.kind == "reduce" and plan.family in NONNEGATIVE_FAMILIES
+              else "false;")]
     for s in plan.scalar_args:
         out.append(f"  float {c_ident(s)};")
     out.append("  __device__ __forceinline__ float operator()(const float* in) const {")

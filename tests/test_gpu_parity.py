@@ -7,9 +7,11 @@ Bar (what a result must meet to pass):
     is specified to, |gpu - ref| <= 1e-6 * max(1, log2 n) * |ref|, with ref
     the oracle's fp64 sum of the fp32 per-element values.  The kernels add
     every value in fp64, so a sum is within about one fp32 rounding of ref
-    whatever the data's cancellation; the largest relative error seen is
-    recorded, and the last test checks it stays within 2^-23 (one fp32 ulp),
-    far inside the bound.
+    whatever the data's cancellation; sums of squares (l2_norm_sq), which
+    cannot cancel, add up to 16 values per tile in fp32 first, which costs
+    at most about 4 fp32 units in the last place.  The largest relative
+    error seen is recorded, and the last test checks it stays within 2^-23
+    (one fp32 ulp), 2^-21 for the sums of squares, far inside the bound.
 """
 
 import math
@@ -236,10 +238,16 @@ def test_loader_rejects_bad_outputs_and_mixed_devices(suite_pkg):
             suite_pkg["dot"](x=x, y=torch.zeros(1000, device="cuda:1"))
 
 
+# sums whose values are never negative (the square family) add within a tile in fp32
+NONNEGATIVE_SUMS = {"l2_norm_sq"}
+
+
 def test_zz_worst_sum_error_is_within_one_fp32_ulp():
     """The sums checked above (when they ran in this session) all came within
-    2^-23 relative of the fp64 reference: the fp32 rounding of the result."""
+    2^-23 relative of the fp64 reference, the fp32 rounding of the result
+    (2^-21 for the sums of squares, whose tiles add in fp32)."""
     if not WORST_REL:
         pytest.skip("no sum was checked in this session")
     print("largest relative sum error per entry:", WORST_REL)
-    assert max(WORST_REL.values()) <= 2.0 ** -23, WORST_REL
+    for entry, rel in WORST_REL.items():
+        assert rel <= (2.0 ** -21 if entry in NONNEGATIVE_SUMS else 2.0 ** -23), (entry, rel)
