@@ -1167,9 +1167,10 @@ def run_strong(args) -> None:
     """Strong scaling: fixed global sizes sharded over the N ranks with
     loom_b200.shard (l2_norm_sq and max_value at N = 2^30; the fused
     pipeline, affine_relu and pipeline_sum, at every --strong-sizes size).
-    Per call: a write-then-read 512 MiB L2 flush, then CUDA events around
-    the call on every rank; a call's time is the max over ranks, and the
-    point's time the median over the calls.  For reductions across GPUs the
+    Per call: a write-then-read 512 MiB L2 flush, a one-element all-reduce
+    that lines the ranks up on the device, then CUDA events around the call
+    on every rank; a call's time is the max over ranks, and the point's time
+    the median over the calls.  For reductions across GPUs the
     peer exchange's wait (from sending this rank's value to holding every
     rank's) is read from the exchange buffer's statistics.  Each point's
     results are checked: sums against the ranks' fp64 sums of the fp32
@@ -1186,6 +1187,7 @@ def run_strong(args) -> None:
     peak, peak_src = read_peak()
     flush = (torch.empty(128 << 20, dtype=torch.float32, device="cuda"),
              torch.ones(128 << 20, dtype=torch.float32, device="cuda"))
+    align = torch.zeros(1, device="cuda")
     configs = [STRONG_L2_MAX] + [("pipeline", ("affine_relu", "pipeline_sum"), k, "uniform")
                                  for k in args.strong_sizes]
     points = []
@@ -1212,6 +1214,12 @@ def run_strong(args) -> None:
             for _ in range(reps):
                 flush[0].fill_(1.0)
                 flush[1].sum()
+                if world > 1:
+                    # line the ranks up on the device: the start events below
+                    # follow a collective that ends on every GPU at once, so a
+                    # rank's flush does not count as the others' exchange wait
+                    import torch.distributed as dist
+                    dist.all_reduce(align)
                 a = torch.cuda.Event(enable_timing=True)
                 b = torch.cuda.Event(enable_timing=True)
                 a.record(stream)

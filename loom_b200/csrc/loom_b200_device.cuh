@@ -79,72 +79,6 @@ __device__ __forceinline__ float load_stream(const float* p) { return __ldcs(p);
 __device__ __forceinline__ void store_stream(float4* p, const float4& v) { __stcs(p, v); }
 __device__ __forceinline__ void store_stream(float* p, float v) { __stcs(p, v); }
 
-// ---------------------------------------------------------------------------
-// the bulk-copy engine (one-input reductions)
-//
-// A one-input reduction streams each tile through shared memory with one
-// cp.async.bulk (global -> this CTA's shared memory, completing on an
-// mbarrier) instead of 1024 16-byte loads: the same bytes in flight, far
-// fewer memory requests.  Measured on B200 at 2^28 it is about 2.6% faster
-// than the register loads for one input and ties for two or three, so only
-// one-input reductions use it.  Only this CTA's own shared memory is ever a
-// destination, and no copy is multicast.
-
-constexpr unsigned kBulkWaitPolls = 1u << 22;   // bound of an mbarrier wait
-
-__device__ __forceinline__ unsigned smem_addr(const void* p) {
-  return (unsigned)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
-               : "memory");
-}
-
-// Makes the barrier's initialisation visible to the bulk-copy (async) proxy.
-__device__ __forceinline__ void fence_mbar_init() {
-  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-}
-
-// Orders this thread's earlier generic-proxy accesses of shared memory (the
-// CTA's reads of the previous tile, after a barrier) before the next bulk
-// copy into the same buffer.
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
-// Thread 0: expect `bytes` on `bar` and copy them from global `src` into
-// shared `dst` (both 16-byte aligned, bytes a multiple of 16).
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, unsigned bytes,
-                                          unsigned long long* bar) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
-               "r"(bytes)
-               : "memory");
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
-}
-
-// Waits for phase `parity` of `bar` to complete, at most kBulkWaitPolls
-// polls; false when the wait ran out.
-__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity) {
-  const unsigned a = smem_addr(bar);
-  for (unsigned polls = 0; polls < kBulkWaitPolls; ++polls) {
-    unsigned done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-  }
-  return false;
-}
-
 // Programmatic dependent launch.  Every kernel here is launched as a
 // programmatic dependent of the kernel before it on the stream.  It first
 // lets its own dependent be scheduled (launch_dependents), then waits for
@@ -297,7 +231,6 @@ struct SumOp {
   }
   static __device__ __forceinline__ double combine(double a, double b) { return __dadd_rn(a, b); }
   static __device__ __forceinline__ float to_float(double a) { return __double2float_rn(a); }
-  static __device__ __forceinline__ double to_acc_nan() { return __longlong_as_double(0x7ff8000000000000ll); }
 };
 
 struct MaxOp {
@@ -311,7 +244,6 @@ struct MaxOp {
   static __device__ __forceinline__ float absorb(float acc, float chunk) { return fmaxf(acc, chunk); }
   static __device__ __forceinline__ float combine(float a, float b) { return fmaxf(a, b); }
   static __device__ __forceinline__ float to_float(float a) { return a; }
-  static __device__ __forceinline__ float to_acc_nan() { return __int_as_float(0x7fc00000); }
 };
 
 // Whether a body's values are never negative: the generated body says so
@@ -451,43 +383,6 @@ reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInp
   const int iters = b < full_tiles ? (int)((full_tiles - 1 - b) / grid + 1) : 0;
   const int64_t stride = grid * kTile;
   Acc acc = Op::init();
-  if constexpr (K == 1) {
-    // one input: every full tile through shared memory by the bulk-copy
-    // engine (see bulk_load); a wait that runs out leaves NaN in the result,
-    // after waiting once more (bounded) for the copy in flight
-    __shared__ __align__(128) float4 tile[kTile];
-    __shared__ __align__(8) unsigned long long bar;
-    __shared__ int bulk_failed;
-    if (threadIdx.x == 0) {
-      mbar_init(&bar, 1);
-      fence_mbar_init();
-      bulk_failed = 0;
-    }
-    __syncthreads();
-    const float4* tile_src = reinterpret_cast<const float4*>(in.p[0] + head) + b * kTile;
-    for (int it = 0; it < iters; ++it) {
-      if (threadIdx.x == 0) {
-        fence_proxy_async_smem();
-        bulk_load(tile, tile_src, kTile * (unsigned)sizeof(float4), &bar);
-      }
-      if (!mbar_wait(&bar, (unsigned)it & 1u)) bulk_failed = 1;
-      float4 v[U][1];
-#pragma unroll
-      for (int u = 0; u < U; ++u) v[u][0] = tile[u * kThreads + threadIdx.x];
-      typename C::T c[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) c[u] = C::chunk4(apply4(body, v[u]));
-      acc = C::absorb(acc, fold_chunks<C, U>(c));
-      __syncthreads();   // every thread has read the tile before the next copy
-      if (bulk_failed) {
-        if (threadIdx.x == 0) mbar_wait(&bar, (unsigned)it & 1u);
-        break;
-      }
-      tile_src += stride;
-      src[0] += stride;
-    }
-    if (bulk_failed) acc = Op::to_acc_nan();
-  } else {
   for (int it = 0; it < iters; ++it) {
     float4 v[U][K];
 #pragma unroll
@@ -500,7 +395,6 @@ reduce_vec_kernel(typename Op::Acc* __restrict__ partials, const Ptrs<Body::kInp
     acc = C::absorb(acc, fold_chunks<C, U>(c));
 #pragma unroll
     for (int k = 0; k < K; ++k) src[k] += stride;
-  }
   }
   // The ragged last tile (tile index full_tiles) is the next tile of CTA
   // full_tiles mod grid, whose pointers now stand at its start.
