@@ -1112,23 +1112,24 @@ def run_workload_sweep(args) -> None:
 STRONG_L2_MAX = ("l2_norm_sq_max", ("l2_norm_sq", "max_value"), 30, "normal_outliers")
 
 
-def global_slice(kind: str, seed: int, start: int, stop: int, chunk: int = 1 << 24):
+def global_slice(kind: str, seed: int, start: int, stop: int, chunk: int = 1 << 24,
+                 device: str = "cuda"):
     """Elements [start, stop) of a seeded global input that does not depend
     on how it is sharded: the global array is cut into fixed chunks, each
     drawn on the device from its own seed, and a rank draws only the chunks
     its shard overlaps."""
     import torch
-    out = torch.empty(stop - start, device="cuda")
-    gen = torch.Generator(device="cuda")
+    out = torch.empty(stop - start, device=device)
+    gen = torch.Generator(device=device)
     c = start // chunk
     while c * chunk < stop:
         lo = c * chunk
         gen.manual_seed(seed * 1000003 + c)
         if kind == "uniform":
-            v = torch.rand(chunk, device="cuda", generator=gen).mul_(2.0).sub_(1.0)
+            v = torch.rand(chunk, device=device, generator=gen).mul_(2.0).sub_(1.0)
         else:
-            v = torch.randn(chunk, device="cuda", generator=gen)
-            v[torch.rand(chunk, device="cuda", generator=gen) < 0.01] *= 1e3
+            v = torch.randn(chunk, device=device, generator=gen)
+            v[torch.rand(chunk, device=device, generator=gen) < 0.01] *= 1e3
         s0, s1 = max(start, lo), min(stop, lo + chunk)
         out[s0 - start:s1 - start] = v[s0 - lo:s1 - lo]
         c += 1

@@ -110,6 +110,23 @@ def test_cpu_inputs_are_the_entries_inputs():
                 assert shared[e][k] == v
 
 
+@pytest.mark.parametrize("kind", ["uniform", "normal_outliers"])
+def test_strong_inputs_do_not_depend_on_the_sharding(kind):
+    # the strong-scaling mode draws the global input in fixed chunks, so the
+    # ranks' shards concatenate to the same array for every world size
+    import torch
+
+    from loom_b200.shard import shard_bounds
+    n, chunk = 10007, 1000
+    whole = bench.global_slice(kind, 5, 0, n, chunk=chunk, device="cpu")
+    for world in (1, 2, 3, 4, 8):
+        parts = [bench.global_slice(kind, 5, a, b, chunk=chunk, device="cpu")
+                 for a, b in shard_bounds(n, world)]
+        assert torch.equal(torch.cat(parts), whole), world
+    if kind == "normal_outliers":
+        assert (whole.abs() > 50).sum() > 0          # the 1% of outliers are there
+
+
 class _FakeProc:
     def terminate(self):
         pass
