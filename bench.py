@@ -350,7 +350,7 @@ def _sum_values(entry: str, data, lo: int, hi: int):
     return z.clamp_min(0.0) * data["u2"][lo:hi]
 
 
-def check_results(data, outs, n: int, world: int, rank: int):
+def check_results(data, outs, n: int, world: int, rank: int, device: str = "cuda"):
     """After the timed region: the results of the last step against
     independent references.  Sums: the ranks' fp64 sums of the fp32
     per-element values, all-reduced, with the bar |got - ref| <= 1e-6 *
@@ -360,7 +360,7 @@ def check_results(data, outs, n: int, world: int, rank: int):
     the host (fmaf formed exactly, relu as x > 0 ? x : 0)."""
     import numpy as np
     import torch
-    local = torch.zeros(3, dtype=torch.float64, device="cuda")
+    local = torch.zeros(3, dtype=torch.float64, device=device)
     chunk = 1 << 26
     for i, e in enumerate(["dot", "l2_norm_sq", "pipeline_sum"]):
         for lo in range(0, n, chunk):
