@@ -7,6 +7,10 @@ bit-exact, sums within 1e-6 * max(1, log2 n) * |ref|):
 * grid sizes 9 (the smallest two-launch grid), 255-257, 4097, and 32768 and
   more tiles (the partial-slot cap, where CTAs take several tiles), aligned
   and with a 3-element head;
+* 889-3553 tiles, where a grid of one to three waves of resident CTAs runs
+  as one wave with several tiles per CTA (on a B200, 888 resident CTAs of
+  the two- and three-input kernels, 1184 of the one-input ones), around
+  both ends of that range; and the number of partials such a call writes;
 * workspaces filled beforehand with zeros, ones, 0xff bytes and random
   bytes: nothing in a workspace has to start at any value;
 * one workspace reused by calls of different sizes and entries: a call
@@ -58,7 +62,8 @@ def call_with_workspace(pkg, entry, dev, ws):
 @pytest.mark.parametrize("entry", ["dot", "l2_norm_sq", "max_value", "pipeline_sum"])
 def test_grid_sizes(suite_pkg, oracle, entry):
     tile = tile_of(entry)
-    sizes = [(9, 0), (9, 5), (255, 1), (256, 0), (256, 1), (257, 0), (4097, 3)]
+    sizes = [(9, 0), (9, 5), (255, 1), (256, 0), (256, 1), (257, 0), (4097, 3),
+             (889, 0), (1185, 3), (1777, 0), (2048, 1), (2665, 0), (3552, 0), (3553, 2)]
     if entry in ("dot", "l2_norm_sq"):
         sizes += [(32768, 0), (32769, 0), (3 * 32768 + 5, 7)]
     for g, d in sizes:
@@ -70,6 +75,42 @@ def test_grid_sizes(suite_pkg, oracle, entry):
                    for k, v in inp.items()}
             got = float(suite_pkg[entry](**dev).cpu()[0])
             check(entry, got, ref, inp, n)
+
+
+def balanced_grid(tiles, wave):
+    """The launcher's grid for a reduction of `tiles` tiles on a device that
+    holds `wave` of its CTAs at once (loom_b200_launch.cuh)."""
+    if tiles <= wave or tiles > 3 * wave:
+        return tiles
+    per_cta = -(-tiles // wave)
+    return -(-tiles // per_cta)
+
+
+def test_mid_grids_run_as_one_wave(suite_pkg, oracle):
+    # The stage writes one partial per CTA (fp64 for sums, fp32 for max) at
+    # the start of the workspace (its first 256-byte boundary); in a workspace
+    # of 0xff bytes the slots it wrote are the ones that changed, and they
+    # must be the grid's prefix.
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    for entry, tiles in (("dot", 2048), ("pipeline_sum", 2048), ("l2_norm_sq", 2000),
+                         ("max_value", 3000)):
+        n = tiles * tile_of(entry) + 1
+        inp = workloads.entry_inputs(entry, n, seed_offset=tiles)
+        dev = {k: (to_device(v) if isinstance(v, np.ndarray) else v) for k, v in inp.items()}
+        ws = _workspace(suite_pkg, entry, n, "ff")
+        check(entry, call_with_workspace(suite_pkg, entry, dev, ws), oracle.run(entry, inp),
+              inp, n)
+        base = (-ws.data_ptr()) % 256
+        slot = np.uint32 if entry == "max_value" else np.uint64
+        raw = ws.cpu().numpy()[base:]
+        slots = raw[:len(raw) // slot().itemsize * slot().itemsize].view(slot)
+        written = np.flatnonzero(slots != np.iinfo(slot).max)
+        grid = len(written)
+        assert np.array_equal(written, np.arange(grid)), (entry, grid)
+        # `tiles` whole tiles (the one extra element is the scalar tail), two
+        # or three per CTA
+        assert grid < tiles, (entry, grid)
+        assert grid in {balanced_grid(tiles, sms * k) for k in range(1, 9)}, (entry, grid)
 
 
 def _workspace(pkg, entry, n, fill):
