@@ -28,7 +28,8 @@
 //    beats a persistent grid-stride loop (SM count x resident CTAs) by 13-16%
 //    for maps and 3-4% for reductions: the static stride leaves the slowest
 //    SMs with the tail.  Map kernels have no loop at all; reductions walk
-//    whole tiles with a grid stride only past kMaxPartials CTAs;
+//    whole tiles with a grid stride past kMaxPartials CTAs, and where the
+//    launcher folds a grid of one to three waves into one balanced wave;
 //  * reductions: sums convert every value to fp64 and accumulate in fp64
 //    (a fixed tree per thread and tile, then a per-thread accumulator);
 //    CTAs reduce with xor-shuffle butterflies and write one fp64 partial each to the caller's
