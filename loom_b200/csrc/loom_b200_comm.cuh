@@ -55,9 +55,16 @@ struct PeerTable {
 //        exchanges of even / odd epoch.  Two sets suffice: a rank can be at
 //        most one exchange ahead of any other, since it cannot finish an
 //        exchange before every rank has sent to it.
+// A slot holds the value's 64 bits as two words, each carrying 32 bits of it
+// (low half in half[0], high half in half[1]) under the low 32 bits of the
+// sender's epoch in its upper half.  An aligned 64-bit store is seen whole
+// or not at all, so a reader that finds this epoch's tag in both words
+// holds the value: the sender needs no release fence (a round trip to the
+// peer) and the reader no acquire.  Epochs start at 1, so a slot still
+// zeroed from creation never matches, and a used slot holds the tag of the
+// exchange two epochs back at worst.
 struct ExchangeSlot {
-  unsigned long long bits;
-  unsigned long long epoch;
+  unsigned long long half[2];
 };
 constexpr size_t kExchangeSlotsOffset = 64;
 constexpr size_t kExchangeBytes = 4096;
@@ -427,12 +434,6 @@ inline int dist_finish<MaxOp>(void*, int64_t, float*, Comm*, cudaStream_t) {
 // ---------------------------------------------------------------------------
 // peer-memory exchange
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 __device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -441,10 +442,6 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long
 
 __device__ __forceinline__ void st_relaxed_sys(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -492,13 +489,13 @@ inline PeerArgs peer_args(const Comm* c, float* out) {
 // The exchange, in every thread of one CTA (`local`, this rank's value, is
 // valid in thread 0; the CTA has at least kMaxRanks threads).  Thread r
 // stores this rank's value into slot [epoch parity][rank] of rank r's
-// exchange buffer (the value, then the epoch with release semantics), then
-// waits until rank r's value of this epoch is in the own buffer (acquire on
-// the epoch) and copies it to shared memory; thread 0 folds the nranks
-// values in rank order into out[0].  The sends and the waits of the ranks
-// run in parallel, one thread per rank: one thread sending to every rank in
-// turn paid a remote release store's round trip per rank (about 2 us each
-// on NVLink, 17-18 us per exchange at 8 GPUs).  The epoch is this rank's own
+// exchange buffer (two epoch-tagged words, relaxed stores), then waits until
+// both words of rank r's slot in the own buffer carry this epoch's tag and
+// copies the value to shared memory; thread 0 folds the nranks values in
+// rank order into out[0].  The sends and the waits of the ranks run in
+// parallel, one thread per rank: one thread sending to every rank in turn
+// paid a remote store's round trip per rank (about 2 us each on NVLink,
+// 17-18 us per exchange at 8 GPUs).  The epoch is this rank's own
 // exchange count, kept in device memory, so it also works when replayed
 // from a graph.  A wait for a peer's value gives up after the
 // communicator's timeout (30 s unless set), records status 1 in the rank's
@@ -529,23 +526,28 @@ __device__ __forceinline__ void exchange_and_fold(const typename Op::Acc local,
   const int set = (int)(epoch & 1ull) * kMaxRanks;
   const int r = (int)threadIdx.x;
   if (r < a.nranks) {
+    const unsigned long long tag = (epoch & 0xffffffffull) << 32;
     ExchangeSlot* s =
         reinterpret_cast<ExchangeSlot*>(a.peers.buf[r] + kExchangeSlotsOffset) + set + a.rank;
-    st_relaxed_sys(&s->bits, x_bits);
-    st_release_sys(&s->epoch, epoch);
-    ExchangeSlot* mine = reinterpret_cast<ExchangeSlot*>(a.own + kExchangeSlotsOffset) + set;
+    st_relaxed_sys(&s->half[0], tag | (x_bits & 0xffffffffull));
+    st_relaxed_sys(&s->half[1], tag | (x_bits >> 32));
+    ExchangeSlot* mine = reinterpret_cast<ExchangeSlot*>(a.own + kExchangeSlotsOffset) + set + r;
     const unsigned long long t0 = global_ns();
     const unsigned long long max_polls = a.timeout_ns / 16 + 1;
     unsigned long long polls = 0;
+    unsigned long long lo = ld_relaxed_sys(&mine->half[0]);
+    unsigned long long hi = ld_relaxed_sys(&mine->half[1]);
     bool ok = true;
-    while (ld_acquire_sys(&mine[r].epoch) != epoch) {
+    while ((lo & ~0xffffffffull) != tag || (hi & ~0xffffffffull) != tag) {
       if (++polls > max_polls || global_ns() - t0 > a.timeout_ns) {
         ok = false;
         break;
       }
       __nanosleep(32);
+      lo = ld_relaxed_sys(&mine->half[0]);
+      hi = ld_relaxed_sys(&mine->half[1]);
     }
-    if (ok) x_vals[r] = ld_relaxed_sys(&mine[r].bits);
+    if (ok) x_vals[r] = ((hi & 0xffffffffull) << 32) | (lo & 0xffffffffull);
     else x_failed = 1;
   }
   __syncthreads();
