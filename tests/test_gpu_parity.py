@@ -43,7 +43,8 @@ WORST_REL = {}
 
 
 def check_sum(entry, got, ref, inp, n):
-    """north_star's bar for a sum: |got - ref| <= 1e-6 * max(1, log2 n) * |ref|."""
+    """The bar for a sum against the oracle's fp64 sum of the same fp32 values:
+    |got - ref| <= 1e-6 * max(1, log2 n) * |ref|."""
     err = abs(got - ref)
     bar = 1e-6 * max(1.0, math.log2(n)) * abs(ref)
     assert err <= bar, (entry, n, got, ref, bar)
